@@ -1,0 +1,547 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 GDN decode path; rank 0 prints one JSON line.
+
+Workload (a "step"): one Gated DeltaNet decode step of a Qwen3-Next-shaped
+layer at batch 256 — 16 q/k heads, 32 v-heads, K = V = 128, T = 1 — with the
+fp32 state [256, 32, 128, 128] (512 MiB) updated in place in HBM.  With
+``--gpus N`` (torchrun, one process per GPU) the 32 v-heads and their 16 q/k
+heads are split across the N ranks (tensor parallel, total work fixed) and
+the bf16 outputs are all-gathered over NVLink by NCCL and head-interleaved.
+
+value   algorithmic HBM bytes of the whole job per second (GB/s): 4,219,008 B
+        per batch entry + 256 B per call, times steps, over the device time of
+        the timed steps (CUDA events, max over ranks).  Inputs are resident
+        in HBM; the 512 MiB state exceeds the 126 MB L2, so no flush is needed.
+e2e     the same metric through the public API (``kernel_cuda_b200`` / the TP
+        step) with the per-step inputs (q, k, v, a, b) copied from pinned host
+        memory and the output read back to the host inside the timed region.
+latency_b1_us   the B=1 decode kernel's median device duration from CUPTI
+        activity records (torch.profiler), L2 flushed before every launch.
+roofline        the decode kernel alone (CUDA events around each launch).
+cpu_baseline    the reference's CPU algorithm (oracle restatement of
+        kernel_pt_reference, its per-head loop) on a bounded sample, host cores.
+
+``--impl reference`` times that CPU implementation alone as the reference arm.
+``--sweep PATH`` also writes a batch sweep (B in 1..256, plus the pooled and
+multi-token configurations) as JSON to PATH.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_ROOT = os.path.join(ROOT, "flashinfer-competition-codebase_b200")
+for _p in (PKG_ROOT, ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "GDN decode µs (CUPTI) at B=1; state-update HBM GB/s vs peak at B=256"
+UNIT = "GB/s"
+BATCH, H, HV, DIM = 256, 16, 32, 128
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "gdn_step_kernel_b256.txt")
+
+# NVML clock-event reason bits
+_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+def log(msg: str) -> None:
+    sys.stderr.write(msg + "\n")
+    sys.stderr.flush()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": FALLBACK_PEAKS["hbm_gbs"], "source": "fallback"}
+
+
+def ncu_traffic_per_launch():
+    """DRAM bytes (read + write) per launch of the B=256 decode kernel, from the
+    committed ncu summary (line ``traffic_bytes_per_launch: N``), else None."""
+    try:
+        with open(PROFILE_SUMMARY) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons of one GPU via NVML in a
+    background thread (every ~2 ms) while the timed region runs."""
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self._stop = threading.Event()
+        self._thread = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            try:
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+                self._h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self._reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # clocks are reported as unavailable
+            log(f"[bench] NVML unavailable: {e}")
+            self.max_mhz = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                rs = self._reasons(self._h)
+                pw = nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0
+                self.samples.append((sm, rs, pw))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def start(self):
+        if self.ok:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        busy = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
+        mask = 0
+        for s in busy:
+            mask |= s[1]
+        return {
+            "sm_mhz": statistics.median(s[0] for s in busy),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": [n for bit, n in _REASONS.items() if mask & bit and bit != 0x1],
+            "power_w_max": round(max(s[2] for s in busy), 1),
+            "samples": len(busy),
+            "source": "nvml",
+        }
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the reference's algorithm on the host cores
+# ---------------------------------------------------------------------------
+
+def cpu_reference_sample(entries: int, seed: int = 0):
+    from gdn_b200 import synthetic
+
+    return synthetic.make_inputs(B=entries, seed=seed)
+
+
+def time_cpu_reference(entries: int, min_seconds: float, max_calls: int = 1000):
+    """Times oracle.decode_loop (the reference's per-head loop) on ``entries``
+    batch entries until ``min_seconds`` elapse; returns (GB/s, seconds, calls)."""
+    from gdn_b200 import synthetic
+    from oracle import gdn_ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    inp = cpu_reference_sample(entries)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        gdn_ref.decode_loop(*inp.args())
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or calls >= max_calls:
+            break
+    gbs = synthetic.bytes_per_call(entries) * calls / el / 1e9
+    return gbs, el, calls
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    from gdn_b200 import synthetic
+    from oracle import gdn_ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    # size each step so the whole run takes about two minutes
+    probe = cpu_reference_sample(1)
+    t0 = time.perf_counter()
+    gdn_ref.decode_loop(*probe.args())
+    per_entry = time.perf_counter() - t0
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    entries = int(max(1, min(BATCH, budget // max(per_entry, 1e-6))))
+    inp = cpu_reference_sample(entries)
+    for _ in range(args.warmup):
+        gdn_ref.decode_loop(*inp.args())
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        gdn_ref.decode_loop(*inp.args())
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    gbs = synthetic.bytes_per_call(entries) * len(times) / total / 1e9
+    sample = (f"{entries} of {BATCH} batch entries (x 32 v-heads) per step, oracle restatement of "
+              f"kernel_pt_reference's per-head loop, torch CPU fp32")
+    line = {
+        "impl": "reference",
+        "metric": METRIC, "value": round(gbs, 6), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / len(times), 3),
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(world),
+        "cpu_baseline": {"value": round(gbs, 6), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+
+def workload_config(world):
+    return {
+        "workload": "gdn_decode_qwen3next_b256_t1",
+        "global_batch": BATCH, "T": 1, "num_qk_heads": H, "num_v_heads": HV, "head_dim": DIM,
+        "state": "fp32 [256,32,128,128] k-last, updated in place",
+        "parallelism": f"tp{world}",
+        "l2": "inputs larger than L2 (512 MiB state per step at N=1; no flush)",
+    }
+
+
+def l2_flush_buffer(device):
+    return torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+
+def cupti_kernel_durations_us(fn, iters, device, name="gdn_step_kernel", flush=None):
+    """Median-ready list of device durations (us) of kernels whose name contains
+    ``name``, from CUPTI activity records (torch.profiler); ``flush`` runs before
+    every launch to empty the L2."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(iters):
+            if flush is not None:
+                flush()
+            fn()
+        torch.cuda.synchronize(device)
+    out = []
+    for e in prof.profiler.kineto_results.events():
+        if name in e.name() and str(e.device_type()).endswith("CUDA"):
+            out.append(e.duration_ns() / 1e3)
+    return out
+
+
+def b1_latency(device, iters=200):
+    import gdn_b200
+    from gdn_b200 import synthetic
+
+    inp = synthetic.make_inputs(B=1, seed=0, device=device)
+    out = torch.empty((1, 1, HV, DIM), dtype=torch.bfloat16, device=device)
+    flush_buf = l2_flush_buffer(device)
+
+    def fn():
+        gdn_b200.kernel_cuda_b200(*inp.args(), out, inp.state)
+
+    for _ in range(20):
+        fn()
+    d = cupti_kernel_durations_us(fn, iters, device, flush=flush_buf.zero_)
+    d_warm = cupti_kernel_durations_us(fn, iters, device, flush=None)
+    res = {"median_us": None, "source": "cupti (torch.profiler activity records)",
+           "l2": "flushed before every launch (256 MiB write)", "iters": len(d)}
+    if d:
+        d.sort()
+        res.update(median_us=round(statistics.median(d), 3), p10_us=round(d[len(d) // 10], 3),
+                   p90_us=round(d[(9 * len(d)) // 10], 3))
+    if d_warm:
+        res["median_us_l2_warm"] = round(statistics.median(d_warm), 3)
+    return res
+
+
+def parity_check(step_inputs, device, step_fn, shard):
+    """Runs one step and compares 4 sampled batch entries (all local heads)
+    with the oracle; returns a summary dict."""
+    from gdn_b200 import synthetic
+    from oracle import gdn_ref
+
+    q, k, v, state, A_log, a, dt_bias, b, scale = step_inputs
+    sel = torch.tensor([0, 1, BATCH // 2, BATCH - 1], device=device)
+    sub = synthetic.GdnInputs(q[sel].cpu(), k[sel].cpu(), v[sel].cpu(), state[sel].cpu(),
+                              A_log.cpu(), a[sel].cpu(), dt_bias.cpu(), b[sel].cpu(), scale)
+    out = step_fn()
+    torch.cuda.synchronize(device)
+    want_out, want_state = gdn_ref.decode(*sub.args())
+    hv0, hv1 = shard.hv0, shard.hv1
+    got_out = out[sel][:, :, hv0:hv1].float().cpu()
+    got_state = state[sel].cpu()
+    e_out = (got_out - want_out.float()).abs()
+    e_st = (got_state - want_state).abs()
+    ok_out = bool(torch.all(e_out <= 1e-2 + 1e-2 * want_out.float().abs()))
+    ok_st = bool(torch.all(e_st <= 1e-3 + 1e-3 * want_state.abs()))
+    return {"sampled_entries": 4, "max_abs_err_output": float(e_out.max()),
+            "max_abs_err_state": float(e_st.max()), "ok": ok_out and ok_st}
+
+
+def run_b200_arm(args, rank, world, local_rank):
+    import gdn_b200
+    from gdn_b200 import synthetic
+    from gdn_b200.tp import HeadShard, TPDecode
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
+    gdn_b200.load_library()
+    shard = HeadShard(rank, world, H, HV)
+    hl, hvl = shard.h_local, shard.hv_local
+
+    # local shard inputs, drawn on the device
+    inp = synthetic.make_inputs(B=BATCH, H=hl, HV=hvl, seed=1234 + rank, device=device)
+    out = torch.empty((BATCH, 1, HV, DIM), dtype=torch.bfloat16, device=device)
+    tp = TPDecode(H=H, HV=HV, max_batch=BATCH, device=device) if world > 1 else None
+
+    def step(events=None):
+        if tp is not None:
+            return tp.step(*inp.args(), out=out, kernel_events=events)
+        if events is not None:
+            events[0].record()
+        gdn_b200.kernel_cuda_b200(*inp.args(), out, inp.state)
+        if events is not None:
+            events[1].record()
+        return out
+
+    parity = parity_check(inp.args(), device, step, shard)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(K)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    wall0 = time.perf_counter()
+    t_start.record()
+    for i in range(K):
+        step(ev[i])
+    t_end.record()
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter() - wall0
+    clocks = sampler.stop()
+    if world > 1:
+        torch.distributed.barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    kernel_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+    elapsed_ms_max = max_over_ranks(elapsed_ms, world, device)
+
+    total_bytes = synthetic.bytes_per_call(BATCH)            # whole job, all heads
+    local_bytes = synthetic.bytes_per_call(BATCH, H=hl, HV=hvl)
+    value = total_bytes * K / (elapsed_ms_max / 1e3) / 1e9
+
+    # end to end through the public API, host buffers in pinned memory
+    host = {n: getattr(inp, n).cpu().pin_memory() for n in ("q", "k", "v", "a", "b")}
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+    K_e2e = max(1, min(K, 500))
+
+    def e2e_step():
+        for n, t in host.items():
+            getattr(inp, n).copy_(t, non_blocking=True)
+        step()
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(K_e2e):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, device)
+    e2e_value = total_bytes * K_e2e / (e2e_ms / 1e3) / 1e9
+
+    latency = b1_latency(device) if (world == 1 and not args.skip_b1) else None
+    sweep = None
+    if args.sweep and world == 1:
+        sweep = run_sweep(device)
+        with open(args.sweep, "w") as f:
+            json.dump(sweep, f, indent=1)
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.skip_cpu:
+        gbs, secs, calls = time_cpu_reference(entries=4, min_seconds=args.cpu_seconds)
+        cpu = {"value": round(gbs, 6), "unit": UNIT, "cores": torch.get_num_threads(),
+               "kind": "port",
+               "sample": f"4 batch entries x 32 v-heads, {calls} calls in {secs:.1f} s "
+                         "(oracle restatement of kernel_pt_reference's per-head loop, torch CPU fp32)"}
+
+    if world > 1:
+        torch.distributed.barrier()
+        del tp
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks = load_peaks()
+    achieved = local_bytes / (kernel_ms / 1e3) / 1e9
+    traffic = ncu_traffic_per_launch() if world == 1 else None
+    launches_per_step = 1 if world == 1 else 2
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(elapsed_ms_max / K, 5),
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
+        "config": workload_config(world),
+        "latency_b1_us": latency,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": traffic, "peak_source": peaks["source"],
+                     "kernel": "gdn_step_kernel", "kernel_us": round(kernel_ms * 1e3, 2),
+                     "algorithmic_bytes_per_launch": local_bytes},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": K_e2e, "api": "gdn_b200.kernel_cuda_b200"
+                if world == 1 else "gdn_b200.tp.TPDecode.step"},
+        "gpu_launches": launches_per_step * K,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+        "parity": parity,
+        "wall_s_timed": round(wall, 4),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_sweep(device):
+    """Batch sweep and the pooled / multi-token configurations (1 GPU)."""
+    import gdn_b200
+    from gdn_b200 import synthetic
+
+    res = {"decode": [], "pooled": None, "mtp": []}
+    for B in (1, 8, 32, 64, 128, 256):
+        inp = synthetic.make_inputs(B=B, seed=B, device=device)
+        out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
+        flush_buf = l2_flush_buffer(device) if B < 64 else None
+        fn = lambda: gdn_b200.kernel_cuda_b200(*inp.args(), out, inp.state)  # noqa: E731
+        for _ in range(10):
+            fn()
+        d = cupti_kernel_durations_us(fn, 100, device,
+                                      flush=None if flush_buf is None else flush_buf.zero_)
+        med = statistics.median(d)
+        nb = synthetic.bytes_per_call(B)
+        res["decode"].append({"B": B, "median_us": round(med, 3), "GBps": round(nb / med / 1e3, 1),
+                              "state_updates_per_s": round(B * HV / (med * 1e-6)),
+                              "l2": "flushed" if flush_buf is not None else "inputs > L2"})
+        del inp, out
+    # pooled: pool of 1024 slots, 256 active entries drawn as a permutation, one -1
+    P, B = 1024, 256
+    inp = synthetic.make_inputs(B=B, slots=P, seed=7, device=device)
+    idx = synthetic.make_pool_indices(B, P, seed=7, n_pad=1, device=device)
+    out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
+    fn = lambda: gdn_b200.gated_delta_rule_decode_pretranspose(  # noqa: E731
+        inp.q, inp.k, inp.v, None, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale, out,
+        use_qk_l2norm=False, initial_state=inp.state, initial_state_indices=idx)
+    for _ in range(10):
+        fn()
+    med = statistics.median(cupti_kernel_durations_us(fn, 50, device))
+    nb = synthetic.bytes_per_call(B, active=B - 1)
+    res["pooled"] = {"pool": P, "B": B, "active": B - 1, "median_us": round(med, 3),
+                     "GBps": round(nb / med / 1e3, 1)}
+    del inp, out
+    for T in (2, 4):
+        B = 64
+        inp = synthetic.make_inputs(B=B, T=T, seed=T, device=device)
+        out = torch.empty((B, T, HV, DIM), dtype=torch.bfloat16, device=device)
+        inter = torch.empty((B, T, HV, DIM, DIM), dtype=torch.float32, device=device)
+        fn = lambda: gdn_b200.gated_delta_rule_mtp(  # noqa: E731
+            inp.q, inp.k, inp.v, inp.state, None, inp.A_log, inp.a, inp.dt_bias, inp.b,
+            inp.scale, out, inter, disable_state_update=False, use_qk_l2norm=False)
+        for _ in range(5):
+            fn()
+        med = statistics.median(cupti_kernel_durations_us(fn, 50, device))
+        nb = synthetic.bytes_per_call(B, T=T, intermediates=True)
+        res["mtp"].append({"B": B, "T": T, "median_us": round(med, 3),
+                           "GBps": round(nb / med / 1e3, 1)})
+        del inp, out, inter
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--sweep", default=None, help="also write the batch sweep JSON here")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
+    ap.add_argument("--skip-b1", action="store_true", help="omit the B=1 latency leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank, world, local_rank = dist_env()
+    if world != args.gpus:
+        log(f"[bench] WORLD_SIZE={world} but --gpus {args.gpus}; using WORLD_SIZE")
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    run_b200_arm(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

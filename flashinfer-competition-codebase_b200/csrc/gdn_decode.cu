@@ -1,0 +1,566 @@
+// gdn_decode.cu — Gated DeltaNet decode kernels for B200 (sm_100a) and their C ABI.
+//
+// The decode step is a batched rank-1 update of an fp32 [V=128, K=128] state per
+// (batch entry, v-head): every state byte is read once and written once, so the
+// path is HBM-bound (about 0.9 flop per byte); it stays on the FP32 pipes and
+// never touches the tensor cores.
+//
+// Work decomposition.  A "row" is one V-row of one head's state: 128 fp32 = 512 B,
+// contiguous in the k-last layout.  A row is owned by a group of LPR lanes
+// (LPR = 8, 16 or 32); lane j of the group holds the 16-byte chunks
+// j, j+LPR, j+2*LPR, ... of the row, so each warp-wide 16-byte load touches
+// 32/LPR whole 128-byte lines.  A lane holds RG rows, a warp RPW = (32/LPR)*RG
+// consecutive rows, a CTA W warps.  One CTA covers RPC = RPW*W rows of one head;
+// the 1-D grid walks (batch, head, row-tile) in memory order.  Every state load
+// of a thread is issued before any arithmetic, so at small batch the kernel
+// costs one DRAM round trip and at large batch the many resident warps keep
+// enough bytes in flight to stream at HBM rate.
+//
+// Arithmetic per row (h = old row, k/q of the row's q/k head, v_r = v[row]):
+//   kh = k.h, qh = q.h              (both on the OLD row: one reduction round)
+//   dv = beta * (v_r - g*kh)        (= new_v - old_v of the reference)
+//   o  = scale * (g*qh + dv*(q.k))  (= scale * q.h_new)
+//   h  = g*h + dv*k
+// which is the reference's sequence old=g*S; old_v=k@old; new_v=beta*v+(1-beta)*old_v;
+// S=old-k*old_v+k*new_v; o=scale*q@S (solution/triton/kernel.py:101-110) with the
+// algebra folded so that both dot products share one warp-shuffle reduction and
+// q.k is computed once per warp instead of once per row.
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/gdn_b200.h"
+
+namespace {
+
+constexpr int kDim = 128;                // K == V == 128 on this path
+constexpr int kHeadElems = kDim * kDim;  // fp32 elements of one head's state
+
+struct StepArgs {
+  const uint16_t* q;        // [B, T, H, K]  bf16
+  const uint16_t* k;        // [B, T, H, K]  bf16
+  const uint16_t* v;        // [B, T, HV, V] bf16
+  const float* state_in;    // [slots, HV, V, K]
+  float* state_out;         // [slots, HV, V, K] (may equal state_in)
+  const float* A_log;       // [HV]
+  const uint16_t* a;        // [B, T, HV] bf16
+  const float* dt_bias;     // [HV]
+  const uint16_t* b;        // [B, T, HV] bf16
+  uint16_t* out;            // [B, T, HV, V] bf16
+  float* inter;             // [B, cache_steps, HV, V, K] or null
+  const int32_t* idx_in;    // [B] read slots, or null (slot = batch entry)
+  const int32_t* idx_out;   // [B] write slots, or null (= read slot)
+  int32_t* bad_count;       // device counter of out-of-range indices, or null
+  float scale;
+  int B, T, H, HV, hv_per_h;
+  int pool;                 // number of slots in state_in/state_out
+  int cache_steps;
+  int l2norm;
+  int write_final;
+};
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ float bf16_to_f32(uint16_t x) {
+  return __uint_as_float(static_cast<uint32_t>(x) << 16);
+}
+__device__ __forceinline__ uint16_t f32_to_bf16(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+// 16-byte state load that does not allocate in L1 (each line is used once).
+__device__ __forceinline__ float4 ld_state(const float* ptr) {
+  float4 r;
+  asm volatile("ld.global.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(ptr)
+               : "memory");
+  return r;
+}
+
+// 16-byte streaming state store (evict-first: the line is not re-read).
+__device__ __forceinline__ void st_state(float* ptr, const float4& x) {
+  asm volatile("st.global.cs.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "f"(x.x), "f"(x.y),
+               "f"(x.z), "f"(x.w)
+               : "memory");
+}
+
+template <int LPR>
+__device__ __forceinline__ float group_sum(float x) {
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// All-reduce of two values over the LPR lanes of a row group with log2(LPR)+1
+// shuffles instead of 2*log2(LPR): the first exchange swaps halves so each half
+// reduces one of the two values, the last exchange hands each half the other sum.
+// All lanes of a group end with bit-identical sums.
+template <int LPR>
+__device__ __forceinline__ void group_sum2(float& x, float& y, int lane) {
+  constexpr int kHalf = LPR / 2;
+  const bool hi = (lane & kHalf) != 0;
+  const float send = hi ? x : y;
+  float keep = hi ? y : x;
+  keep += __shfl_xor_sync(0xffffffffu, send, kHalf);
+#pragma unroll
+  for (int o = kHalf / 2; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+  const float other = __shfl_xor_sync(0xffffffffu, keep, kHalf);
+  x = hi ? other : keep;
+  y = hi ? keep : other;
+}
+
+// softplus with PyTorch's default threshold (x > 20 returns x), as in
+// solution/triton/kernel.py:74 (F.softplus) and :290.
+__device__ __forceinline__ float softplus_f(float x) {
+  return x > 20.0f ? x : log1pf(expf(x));
+}
+
+// Per-token inputs of one warp, kept packed until they are used so that the
+// next token's loads can be in flight while this token computes.
+template <int NC, int RG>
+struct TokenRaw {
+  uint2 q[NC];
+  uint2 k[NC];
+  uint16_t v[RG];
+  uint16_t a, b;
+};
+
+// One kernel body for every variant of the step:
+//   TT == 1: single token (decode), TT == 0: T tokens from p.T (multi-token).
+template <int LPR, int RG, int W, int TT>
+__global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
+  constexpr int kGroups = 32 / LPR;     // row groups per warp
+  constexpr int kRPW = kGroups * RG;    // rows per warp
+  constexpr int kRPC = kRPW * W;        // rows per CTA
+  constexpr int kEPL = kDim / LPR;      // fp32 elements per lane per row
+  constexpr int kNC = kEPL / 4;         // 16-byte chunks per lane per row
+  constexpr int kTPH = kDim / kRPC;     // CTAs per head
+  static_assert(kDim % kRPC == 0, "rows per CTA must divide V");
+
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int gl = lane & (LPR - 1);
+  const int grp = lane / LPR;
+
+  const int bh = blockIdx.x / kTPH;
+  const int tile_in_head = blockIdx.x - bh * kTPH;
+  const int row0 = tile_in_head * kRPC + warp * kRPW + grp;  // row of r is row0 + r*kGroups
+  const int bi = bh / p.HV;
+  const int hv = bh - bi * p.HV;
+  const int hq = hv / p.hv_per_h;
+  const int T = TT ? TT : p.T;
+
+  // ---- slots -------------------------------------------------------------
+  int slot_in = bi;
+  int slot_out = bi;
+  bool active = true;
+  bool do_write = p.write_final != 0;
+  if (p.idx_in != nullptr) {
+    slot_in = __ldg(p.idx_in + bi);
+    const bool counted = (hv == 0 && tile_in_head == 0 && threadIdx.x == 0);
+    if (slot_in < 0 || slot_in >= p.pool) {
+      if (slot_in >= p.pool && counted && p.bad_count) atomicAdd(p.bad_count, 1);
+      active = false;
+    }
+    slot_out = slot_in;
+    if (active && p.idx_out != nullptr) {
+      slot_out = __ldg(p.idx_out + bi);
+      if (slot_out < 0) {
+        slot_out = 0;  // null-buffer convention of the pool API
+      } else if (slot_out >= p.pool) {
+        if (counted && p.bad_count) atomicAdd(p.bad_count, 1);
+        do_write = false;
+      }
+    }
+  }
+
+  // ---- state loads first: the only large transfer -------------------------
+  float4 h[RG][kNC];
+  if (active) {
+    const float* src = p.state_in + (static_cast<size_t>(slot_in) * p.HV + hv) * kHeadElems +
+                       static_cast<size_t>(row0) * kDim + gl * 4;
+#pragma unroll
+    for (int r = 0; r < RG; ++r)
+#pragma unroll
+      for (int c = 0; c < kNC; ++c) h[r][c] = ld_state(src + r * kGroups * kDim + c * LPR * 4);
+  }
+
+  auto load_token = [&](int t, TokenRaw<kNC, RG>& raw) {
+    const size_t bt = static_cast<size_t>(bi) * T + t;
+    const uint2* qp = reinterpret_cast<const uint2*>(p.q + (bt * p.H + hq) * kDim + gl * 4);
+    const uint2* kp = reinterpret_cast<const uint2*>(p.k + (bt * p.H + hq) * kDim + gl * 4);
+#pragma unroll
+    for (int c = 0; c < kNC; ++c) {
+      raw.q[c] = __ldg(qp + c * LPR);
+      raw.k[c] = __ldg(kp + c * LPR);
+    }
+    const uint16_t* vp = p.v + (bt * p.HV + hv) * kDim + row0;
+#pragma unroll
+    for (int r = 0; r < RG; ++r) raw.v[r] = __ldg(vp + r * kGroups);
+    raw.a = __ldg(p.a + bt * p.HV + hv);
+    raw.b = __ldg(p.b + bt * p.HV + hv);
+  };
+
+  TokenRaw<kNC, RG> cur;
+  load_token(0, cur);
+  const float neg_exp_A = -expf(__ldg(p.A_log + hv));
+  const float dt_b = __ldg(p.dt_bias + hv);
+
+  for (int t = 0; t < T; ++t) {
+    TokenRaw<kNC, RG> nxt;
+    if (TT != 1 && t + 1 < T) load_token(t + 1, nxt);
+
+    // Gates (solution/triton/kernel.py:73-75): g = exp(-exp(A_log)*softplus(a+dt_bias)),
+    // beta = sigmoid(b).
+    const float g = expf(neg_exp_A * softplus_f(bf16_to_f32(cur.a) + dt_b));
+    const float beta = 1.0f / (1.0f + expf(-bf16_to_f32(cur.b)));
+
+    float qf[kEPL], kf[kEPL];
+#pragma unroll
+    for (int c = 0; c < kNC; ++c) {
+      qf[4 * c + 0] = bf16_lo(cur.q[c].x);
+      qf[4 * c + 1] = bf16_hi(cur.q[c].x);
+      qf[4 * c + 2] = bf16_lo(cur.q[c].y);
+      qf[4 * c + 3] = bf16_hi(cur.q[c].y);
+      kf[4 * c + 0] = bf16_lo(cur.k[c].x);
+      kf[4 * c + 1] = bf16_hi(cur.k[c].x);
+      kf[4 * c + 2] = bf16_lo(cur.k[c].y);
+      kf[4 * c + 3] = bf16_hi(cur.k[c].y);
+    }
+    float qk = 0.0f;
+#pragma unroll
+    for (int e = 0; e < kEPL; ++e) qk = fmaf(qf[e], kf[e], qk);
+    if (p.l2norm) {
+      // x * rsqrt(sum(x^2) + 1e-6), the convention of
+      // flashinfer/gdn_kernels/gdn_decode_pretranspose.py:253-254.
+      float qq = 0.0f, kk = 0.0f;
+#pragma unroll
+      for (int e = 0; e < kEPL; ++e) {
+        qq = fmaf(qf[e], qf[e], qq);
+        kk = fmaf(kf[e], kf[e], kk);
+      }
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) {
+        qq += __shfl_xor_sync(0xffffffffu, qq, o);
+        kk += __shfl_xor_sync(0xffffffffu, kk, o);
+        qk += __shfl_xor_sync(0xffffffffu, qk, o);
+      }
+      const float rq = rsqrtf(qq + 1e-6f);
+      const float rk = rsqrtf(kk + 1e-6f);
+#pragma unroll
+      for (int e = 0; e < kEPL; ++e) {
+        qf[e] *= rq;
+        kf[e] *= rk;
+      }
+      qk *= rq * rk;
+    } else {
+      qk = group_sum<LPR>(qk);
+    }
+#pragma unroll
+    for (int e = 0; e < kEPL; ++e) qf[e] *= p.scale;
+    qk *= p.scale;
+
+    const size_t bt = static_cast<size_t>(bi) * T + t;
+    uint16_t* op = p.out + (bt * p.HV + hv) * kDim + row0;
+    if (active) {
+#pragma unroll
+      for (int r = 0; r < RG; ++r) {
+        float kh0 = 0.0f, kh1 = 0.0f, qh0 = 0.0f, qh1 = 0.0f;
+#pragma unroll
+        for (int c = 0; c < kNC; ++c) {
+          kh0 = fmaf(kf[4 * c + 0], h[r][c].x, kh0);
+          kh1 = fmaf(kf[4 * c + 1], h[r][c].y, kh1);
+          kh0 = fmaf(kf[4 * c + 2], h[r][c].z, kh0);
+          kh1 = fmaf(kf[4 * c + 3], h[r][c].w, kh1);
+          qh0 = fmaf(qf[4 * c + 0], h[r][c].x, qh0);
+          qh1 = fmaf(qf[4 * c + 1], h[r][c].y, qh1);
+          qh0 = fmaf(qf[4 * c + 2], h[r][c].z, qh0);
+          qh1 = fmaf(qf[4 * c + 3], h[r][c].w, qh1);
+        }
+        float kh = kh0 + kh1;
+        float qh = qh0 + qh1;
+        group_sum2<LPR>(kh, qh, lane);
+        const float dv = beta * (bf16_to_f32(cur.v[r]) - g * kh);
+        const float o = fmaf(g, qh, dv * qk);
+#pragma unroll
+        for (int c = 0; c < kNC; ++c) {
+          h[r][c].x = fmaf(dv, kf[4 * c + 0], g * h[r][c].x);
+          h[r][c].y = fmaf(dv, kf[4 * c + 1], g * h[r][c].y);
+          h[r][c].z = fmaf(dv, kf[4 * c + 2], g * h[r][c].z);
+          h[r][c].w = fmaf(dv, kf[4 * c + 3], g * h[r][c].w);
+        }
+        if (gl == 0) op[r * kGroups] = f32_to_bf16(o);
+      }
+      if (TT != 1 && p.inter != nullptr) {
+        float* ip = p.inter + ((static_cast<size_t>(bi) * p.cache_steps + t) * p.HV + hv) * kHeadElems +
+                    static_cast<size_t>(row0) * kDim + gl * 4;
+#pragma unroll
+        for (int r = 0; r < RG; ++r)
+#pragma unroll
+          for (int c = 0; c < kNC; ++c) st_state(ip + r * kGroups * kDim + c * LPR * 4, h[r][c]);
+      }
+    } else if (gl == 0) {
+#pragma unroll
+      for (int r = 0; r < RG; ++r) op[r * kGroups] = 0;
+    }
+    if (TT != 1) cur = nxt;
+  }
+
+  if (active && do_write) {
+    float* dst = p.state_out + (static_cast<size_t>(slot_out) * p.HV + hv) * kHeadElems +
+                 static_cast<size_t>(row0) * kDim + gl * 4;
+#pragma unroll
+    for (int r = 0; r < RG; ++r)
+#pragma unroll
+      for (int c = 0; c < kNC; ++c) st_state(dst + r * kGroups * kDim + c * LPR * 4, h[r][c]);
+  }
+}
+
+// Tensor-parallel head interleave: gathered [W, rows, HVl, V] -> out [rows, W*HVl, V],
+// moved as 8-byte words (V % 4 == 0).
+__global__ void interleave_heads_kernel(const uint2* __restrict__ src, uint2* __restrict__ dst,
+                                        int world, int rows, int hvl, int v4) {
+  const size_t per_rank = static_cast<size_t>(rows) * hvl * v4;
+  const size_t total = per_rank * world;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t w = i / per_rank;
+    const size_t rem = i - w * per_rank;
+    const size_t r = rem / (static_cast<size_t>(hvl) * v4);
+    const size_t jv = rem - r * hvl * v4;  // j * v4 + e
+    dst[(r * world + w) * hvl * v4 + jv] = src[i];
+  }
+}
+
+// ---- host side --------------------------------------------------------------
+
+struct LaunchShape {
+  int lpr, rg, warps;
+};
+
+template <int LPR, int RG, int W, int TT>
+cudaError_t launch_step(const StepArgs& p, cudaStream_t stream) {
+  constexpr int kRPC = (32 / LPR) * RG * W;
+  const long long ctas = static_cast<long long>(p.B) * p.HV * (kDim / kRPC);
+  gdn_step_kernel<LPR, RG, W, TT><<<static_cast<unsigned>(ctas), W * 32, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+using LaunchFn = cudaError_t (*)(const StepArgs&, cudaStream_t);
+
+template <int TT>
+LaunchFn pick_launch(LaunchShape s) {
+#define GDN_SHAPE(L, R, W) \
+  if (s.lpr == L && s.rg == R && s.warps == W) return &launch_step<L, R, W, TT>;
+#define GDN_SHAPES_W(L, R) GDN_SHAPE(L, R, 1) GDN_SHAPE(L, R, 2) GDN_SHAPE(L, R, 4) GDN_SHAPE(L, R, 8)
+#define GDN_SHAPES_R(L) GDN_SHAPES_W(L, 1) GDN_SHAPES_W(L, 2) GDN_SHAPES_W(L, 4)
+  GDN_SHAPES_R(8)
+  GDN_SHAPES_R(16)
+  GDN_SHAPES_R(32)
+#undef GDN_SHAPES_R
+#undef GDN_SHAPES_W
+#undef GDN_SHAPE
+  return nullptr;
+}
+
+// Launch shape by regime.  Small batch is latency-bound: many small CTAs spread
+// the rows over all 148 SMs so each SM issues a few KB of loads at once.
+// Large batch is bandwidth-bound: bigger CTAs, two rows per lane.
+LaunchShape default_shape(long long heads, int T) {
+  if (T > 1) return LaunchShape{8, 1, 4};
+  if (heads <= 256) return LaunchShape{8, 1, 1};
+  return LaunchShape{8, 2, 4};
+}
+
+bool aligned(const void* ptr, size_t n) { return (reinterpret_cast<uintptr_t>(ptr) % n) == 0; }
+
+bool overlaps(const void* a, size_t na, const void* b, size_t nb) {
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(a), pb = reinterpret_cast<uintptr_t>(b);
+  return pa < pb + nb && pb < pa + na;
+}
+
+float resolve_scale(double scale, int K) {
+  return (scale == 0.0) ? static_cast<float>(1.0 / sqrt(static_cast<double>(K))) : static_cast<float>(scale);
+}
+
+int check_common(const void* q, const void* k, const void* v, const void* state, const void* A_log,
+                 const void* a, const void* dt_bias, const void* b, const void* output, int B, int T,
+                 int H, int HV, int K, int V, long long slots) {
+  if (!q || !k || !v || !state || !A_log || !a || !dt_bias || !b || !output) return GDN_ERR_NULL;
+  if (K != kDim || V != kDim) return GDN_ERR_SHAPE;
+  if (B < 0 || T < 1 || H < 1 || HV < 1 || HV % H != 0 || slots < 1) return GDN_ERR_SHAPE;
+  // grid size and 32-bit index products stay in range
+  if (static_cast<long long>(B) * HV * kDim > 0x7fffffffLL) return GDN_ERR_SHAPE;
+  if (static_cast<long long>(B) * T * H > 0x7fffffffLL / kDim) return GDN_ERR_SHAPE;
+  if (!aligned(state, 16) || !aligned(q, 8) || !aligned(k, 8) || !aligned(v, 2) ||
+      !aligned(a, 2) || !aligned(b, 2) || !aligned(output, 2) || !aligned(A_log, 4) ||
+      !aligned(dt_bias, 4))
+    return GDN_ERR_ALIGN;
+  return GDN_OK;
+}
+
+int run(const StepArgs& p, LaunchShape shape, int TT, cudaStream_t stream) {
+  if (p.B == 0) return GDN_OK;
+  LaunchFn fn = (TT == 1) ? pick_launch<1>(shape) : pick_launch<0>(shape);
+  if (!fn) return GDN_ERR_SHAPE;
+  return fn(p, stream) == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+StepArgs make_args(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const float* state_in,
+                   float* state_out, const float* A_log, const gdn_bf16* a, const float* dt_bias,
+                   const gdn_bf16* b, double scale, gdn_bf16* output, int B, int T, int H, int HV,
+                   int K, int pool, int use_qk_l2norm) {
+  StepArgs p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.state_in = state_in;
+  p.state_out = state_out;
+  p.A_log = A_log;
+  p.a = a;
+  p.dt_bias = dt_bias;
+  p.b = b;
+  p.out = output;
+  p.scale = resolve_scale(scale, K);
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.HV = HV;
+  p.hv_per_h = HV / H;
+  p.pool = pool;
+  p.cache_steps = T;
+  p.l2norm = use_qk_l2norm ? 1 : 0;
+  p.write_final = 1;
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gdn_abi_version(void) { return GDN_ABI_VERSION; }
+
+const char* gdn_strerror(int code) {
+  switch (code) {
+    case GDN_OK: return "ok";
+    case GDN_ERR_NULL: return "a required pointer is NULL";
+    case GDN_ERR_SHAPE: return "unsupported or inconsistent sizes (K and V must be 128, HV a multiple of H)";
+    case GDN_ERR_ALIGN: return "misaligned pointer (state needs 16 B, q/k 8 B, fp32 vectors 4 B, bf16 2 B)";
+    case GDN_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case GDN_ERR_ALIAS: return "state and new_state overlap without being the same buffer";
+    default: return "unknown gdn error code";
+  }
+}
+
+int gdn_decode(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const float* state,
+               const float* A_log, const gdn_bf16* a, const float* dt_bias, const gdn_bf16* b,
+               double scale, gdn_bf16* output, float* new_state, int B, int H, int HV, int K, int V,
+               int use_qk_l2norm, void* stream) {
+  const int rc = check_common(q, k, v, state, A_log, a, dt_bias, b, output, B, 1, H, HV, K, V,
+                              B > 0 ? B : 1);
+  if (rc != GDN_OK) return rc;
+  if (!new_state) return GDN_ERR_NULL;
+  if (!aligned(new_state, 16)) return GDN_ERR_ALIGN;
+  const size_t bytes = static_cast<size_t>(B) * HV * kHeadElems * sizeof(float);
+  if (state != new_state && overlaps(state, bytes, new_state, bytes)) return GDN_ERR_ALIAS;
+  StepArgs p = make_args(q, k, v, state, new_state, A_log, a, dt_bias, b, scale, output, B, 1, H,
+                         HV, K, B, use_qk_l2norm);
+  return run(p, default_shape(static_cast<long long>(B) * HV, 1), 1,
+             static_cast<cudaStream_t>(stream));
+}
+
+int gdn_decode_pooled(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float* state_pool,
+                      int pool_size, const int32_t* state_indices,
+                      const int32_t* output_state_indices, const float* A_log, const gdn_bf16* a,
+                      const float* dt_bias, const gdn_bf16* b, double scale, gdn_bf16* output,
+                      int B, int H, int HV, int K, int V, int use_qk_l2norm,
+                      int32_t* bad_index_count, void* stream) {
+  const int rc = check_common(q, k, v, state_pool, A_log, a, dt_bias, b, output, B, 1, H, HV, K,
+                              V, pool_size);
+  if (rc != GDN_OK) return rc;
+  if (!state_indices) return GDN_ERR_NULL;
+  if (!aligned(state_indices, 4) || !aligned(output_state_indices, 4) ||
+      !aligned(bad_index_count, 4))
+    return GDN_ERR_ALIGN;
+  StepArgs p = make_args(q, k, v, state_pool, state_pool, A_log, a, dt_bias, b, scale, output, B,
+                         1, H, HV, K, pool_size, use_qk_l2norm);
+  p.idx_in = state_indices;
+  p.idx_out = output_state_indices;
+  p.bad_count = bad_index_count;
+  return run(p, default_shape(static_cast<long long>(B) * HV, 1), 1,
+             static_cast<cudaStream_t>(stream));
+}
+
+int gdn_decode_mtp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float* state_pool,
+                   int pool_size, const int32_t* state_indices, const float* A_log,
+                   const gdn_bf16* a, const float* dt_bias, const gdn_bf16* b, double scale,
+                   gdn_bf16* output, float* intermediate_states, int cache_steps,
+                   int disable_state_update, int B, int T, int H, int HV, int K, int V,
+                   int use_qk_l2norm, int32_t* bad_index_count, void* stream) {
+  const int rc = check_common(q, k, v, state_pool, A_log, a, dt_bias, b, output, B, T, H, HV, K,
+                              V, pool_size);
+  if (rc != GDN_OK) return rc;
+  if (!state_indices && pool_size < B) return GDN_ERR_SHAPE;
+  if (intermediate_states && cache_steps < T) return GDN_ERR_SHAPE;
+  if (!aligned(state_indices, 4) || !aligned(intermediate_states, 16) ||
+      !aligned(bad_index_count, 4))
+    return GDN_ERR_ALIGN;
+  StepArgs p = make_args(q, k, v, state_pool, state_pool, A_log, a, dt_bias, b, scale, output, B,
+                         T, H, HV, K, pool_size, use_qk_l2norm);
+  p.idx_in = state_indices;
+  p.bad_count = bad_index_count;
+  p.inter = intermediate_states;
+  p.cache_steps = intermediate_states ? cache_steps : T;
+  p.write_final = disable_state_update ? 0 : 1;
+  if (T == 1 && !intermediate_states)
+    return run(p, default_shape(static_cast<long long>(B) * HV, 1), 1,
+               static_cast<cudaStream_t>(stream));
+  return run(p, default_shape(static_cast<long long>(B) * HV, T), 0,
+             static_cast<cudaStream_t>(stream));
+}
+
+int gdn_decode_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float* state_pool,
+                     int pool_size, const int32_t* state_indices, const float* A_log,
+                     const gdn_bf16* a, const float* dt_bias, const gdn_bf16* b, double scale,
+                     gdn_bf16* output, int B, int T, int H, int HV, int K, int V,
+                     int use_qk_l2norm, int lanes_per_row, int rows_per_lane, int warps_per_cta,
+                     void* stream) {
+  const int rc = check_common(q, k, v, state_pool, A_log, a, dt_bias, b, output, B, T, H, HV, K,
+                              V, pool_size);
+  if (rc != GDN_OK) return rc;
+  if (!state_indices && pool_size < B) return GDN_ERR_SHAPE;
+  if (!aligned(state_indices, 4)) return GDN_ERR_ALIGN;
+  StepArgs p = make_args(q, k, v, state_pool, state_pool, A_log, a, dt_bias, b, scale, output, B,
+                         T, H, HV, K, pool_size, use_qk_l2norm);
+  p.idx_in = state_indices;
+  LaunchShape s = default_shape(static_cast<long long>(B) * HV, T);
+  if (lanes_per_row > 0) s.lpr = lanes_per_row;
+  if (rows_per_lane > 0) s.rg = rows_per_lane;
+  if (warps_per_cta > 0) s.warps = warps_per_cta;
+  return run(p, s, T == 1 ? 1 : 0, static_cast<cudaStream_t>(stream));
+}
+
+int gdn_interleave_heads(const gdn_bf16* gathered, gdn_bf16* output, int world, int rows, int HVl,
+                         int V, void* stream) {
+  if (!gathered || !output) return GDN_ERR_NULL;
+  if (world < 1 || rows < 0 || HVl < 1 || V < 4 || V % 4 != 0) return GDN_ERR_SHAPE;
+  if (!aligned(gathered, 8) || !aligned(output, 8)) return GDN_ERR_ALIGN;
+  const size_t n = static_cast<size_t>(world) * rows * HVl * V;
+  if (overlaps(gathered, n * 2, output, n * 2)) return GDN_ERR_ALIAS;
+  if (rows == 0) return GDN_OK;
+  const size_t words = n / 4;
+  const int threads = 256;
+  size_t blocks = (words + threads - 1) / threads;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  interleave_heads_kernel<<<static_cast<unsigned>(blocks), threads, 0,
+                            static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint2*>(gathered), reinterpret_cast<uint2*>(output), world, rows, HVl,
+      V / 4);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+}  // extern "C"

@@ -1,0 +1,176 @@
+/*
+ * gdn_b200.h — C ABI of the B200 (sm_100a) Gated DeltaNet decode library.
+ *
+ * One library, libgdn_b200.so, holds every kernel of the GDN decode path:
+ * the fused T=1 decode step, the pooled-state (continuous batching) step,
+ * the multi-token (speculative verify) step and the head interleave used
+ * after a tensor-parallel all-gather.  No function here allocates memory:
+ * the caller owns every buffer.  No function synchronises the host: work
+ * is enqueued on the given stream (NULL = the legacy default stream).
+ *
+ * Data layout (all tensors contiguous, row-major):
+ *   q, k        [B, T, H,  K]   bf16
+ *   v           [B, T, HV, V]   bf16
+ *   a, b        [B, T, HV]      bf16   (decay input, update-gate input)
+ *   A_log       [HV]            fp32
+ *   dt_bias     [HV]            fp32
+ *   state       [S, HV, V, K]   fp32   "k-last": K is the contiguous axis
+ *   output      [B, T, HV, V]   bf16
+ * with K == V == 128, HV % H == 0 (v-head hv reads q/k head hv / (HV/H)).
+ *
+ * Per (batch, v-head) and token, with x = a + dt_bias:
+ *   g    = exp(-exp(A_log) * softplus(x))   softplus(x) = x if x > 20
+ *   beta = sigmoid(b)
+ *   S    = g * S + k (beta * (v - k.(g S)))^T     (delta rule, rank 1)
+ *   o    = scale * S^T q
+ * Optional q/k L2 normalisation: x * rsqrt(sum(x^2) + 1e-6).
+ *
+ * Return value: GDN_OK (0) or a negative GDN_ERR_* code.  Argument errors
+ * are detected before anything is enqueued; GDN_ERR_LAUNCH reports a
+ * failed kernel launch (cudaGetLastError after the launch).
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* bf16 values travel as their 16-bit pattern. */
+typedef uint16_t gdn_bf16;
+
+/* Exported symbols stay visible when the library is built with
+ * -fvisibility=hidden. */
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+#define GDN_OK 0
+#define GDN_ERR_NULL (-1)        /* a required pointer is NULL            */
+#define GDN_ERR_SHAPE (-2)       /* unsupported or inconsistent sizes     */
+#define GDN_ERR_ALIGN (-3)       /* a pointer is not suitably aligned     */
+#define GDN_ERR_LAUNCH (-4)      /* the CUDA launch failed                */
+#define GDN_ERR_ALIAS (-5)       /* in/out buffers overlap illegally      */
+
+#define GDN_ABI_VERSION 1
+
+/* Version of this ABI (GDN_ABI_VERSION of the build). */
+GDN_API int gdn_abi_version(void);
+
+/* Human-readable text for a GDN_* return code (static storage). */
+GDN_API const char* gdn_strerror(int code);
+
+/*
+ * Fused T=1 decode step, destination-passing form.
+ *
+ * Replaces the reference's TVM-FFI exports `kernel_cuda` / `kernel_cuda_v4`
+ * (solution/cuda/kernel.cu:216-254 and :405-443, bound in Python by
+ * solution/cuda/binding.py:35-60) and the Triton entry `kernel_fla_recurrent`
+ * (solution/triton/kernel.py:150-197): same tensors, same argument order.
+ * `state` is read, `new_state` is written; they may be the same buffer
+ * (in-place update, the usual case) or fully disjoint.  scale == 0 selects
+ * 1/sqrt(K) (solution/cuda/binding.py:38-41).  `use_qk_l2norm` != 0 also
+ * L2-normalises q and k (the reference path passes False).
+ * Sizes: state/new_state hold B slots, T == 1.
+ */
+GDN_API int gdn_decode(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+               const float* state, const float* A_log, const gdn_bf16* a,
+               const float* dt_bias, const gdn_bf16* b, double scale,
+               gdn_bf16* output, float* new_state,
+               int B, int H, int HV, int K, int V,
+               int use_qk_l2norm, void* stream);
+
+/*
+ * Pooled-state T=1 decode (continuous batching), updating the pool in place.
+ *
+ * Replaces the float32 pool path of FlashInfer's
+ * gated_delta_rule_decode_pretranspose(initial_state=..., initial_state_indices=...,
+ * output_state_indices=...) (flashinfer/gdn_decode.py:118-195, kernel side
+ * flashinfer/gdn_kernels/gdn_decode_pretranspose.py:136-160), which the
+ * reference calls from kernel_fi_baseline (solution/triton/kernel.py:124-147).
+ * Batch entry i reads slot state_indices[i] of `state_pool` [pool_size,HV,V,K].
+ *  - state_indices[i] < 0: entry skipped, pool untouched, output rows zero.
+ *  - state_indices[i] >= pool_size: treated like -1 and counted in
+ *    *bad_index_count (device int32, may be NULL) so a caller can detect it.
+ *  - output_state_indices (may be NULL = same slot): the updated state is
+ *    written to slot output_state_indices[i]; a negative value redirects the
+ *    write to slot 0 (FlashInfer's null-buffer convention); a value >=
+ *    pool_size skips the write and is counted in *bad_index_count.
+ * Active read slots must be distinct, and so must active write slots: two
+ * entries sharing a slot race.
+ */
+GDN_API int gdn_decode_pooled(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                      float* state_pool, int pool_size,
+                      const int32_t* state_indices,
+                      const int32_t* output_state_indices,
+                      const float* A_log, const gdn_bf16* a,
+                      const float* dt_bias, const gdn_bf16* b, double scale,
+                      gdn_bf16* output, int B, int H, int HV, int K, int V,
+                      int use_qk_l2norm, int32_t* bad_index_count,
+                      void* stream);
+
+/*
+ * Multi-token (T >= 1) sequential decode for speculative verification.
+ *
+ * Replaces FlashInfer's gated_delta_rule_mtp (flashinfer/gdn_decode.py:557-700);
+ * the per-token recurrence is the reference's kernel_prefill_reference inner
+ * loop (solution/triton/prefill_kernel.py:142-181) applied to T tokens.
+ * Entry i starts from slot s = state_indices ? state_indices[i] : i of
+ * `state_pool` [pool_size,HV,V,K] and runs tokens t = 0..T-1 of q/k/v/a/b
+ * ([B,T,...]).  After token t the state is written to
+ * intermediate_states[i, t] ([B, cache_steps, HV, V, K], cache_steps >= T,
+ * indexed by batch entry like FlashInfer's kernel,
+ * flashinfer/gdn_kernels/gdn_decode_mtp.py:645) when that pointer is
+ * non-NULL.  Unless disable_state_update != 0 the final state is written
+ * back to slot s.  Slots < 0 (or >= pool_size, counted in *bad_index_count)
+ * are skipped with zero outputs and untouched intermediates.
+ */
+GDN_API int gdn_decode_mtp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                   float* state_pool, int pool_size,
+                   const int32_t* state_indices,
+                   const float* A_log, const gdn_bf16* a,
+                   const float* dt_bias, const gdn_bf16* b, double scale,
+                   gdn_bf16* output, float* intermediate_states,
+                   int cache_steps, int disable_state_update,
+                   int B, int T, int H, int HV, int K, int V,
+                   int use_qk_l2norm, int32_t* bad_index_count,
+                   void* stream);
+
+/*
+ * Launch-shape tuning entry (no counterpart in the reference, whose launch
+ * shapes are fixed: solution/cuda/kernel.cu:234-235, :423-424).  Same step
+ * as gdn_decode_mtp without intermediates (T == 1: gdn_decode_pooled with
+ * state_indices, or gdn_decode in place when state_indices is NULL), with
+ * an explicit work split: lanes_per_row in {8,16,32} lanes share one 512-byte
+ * state row, rows_per_lane in {1,2,4}, warps_per_cta in {1,2,4,8}; 0 keeps
+ * the library's default for that field.  Used by the benchmark's sweeps.
+ */
+GDN_API int gdn_decode_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                     float* state_pool, int pool_size,
+                     const int32_t* state_indices,
+                     const float* A_log, const gdn_bf16* a,
+                     const float* dt_bias, const gdn_bf16* b, double scale,
+                     gdn_bf16* output, int B, int T, int H, int HV, int K,
+                     int V, int use_qk_l2norm, int lanes_per_row,
+                     int rows_per_lane, int warps_per_cta, void* stream);
+
+/*
+ * Head interleave after a tensor-parallel output all-gather.
+ *
+ * No counterpart in the reference (it runs on one GPU only).  Rank r of W
+ * owns v-heads [r*HVl, (r+1)*HVl); an all-gather of the per-rank outputs
+ * [rows, HVl, V] yields `gathered` [W, rows, HVl, V]; this writes
+ * `output` [rows, W*HVl, V] (rows = B*T).
+ */
+GDN_API int gdn_interleave_heads(const gdn_bf16* gathered, gdn_bf16* output,
+                         int world, int rows, int HVl, int V, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */

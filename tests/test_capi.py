@@ -1,0 +1,135 @@
+"""The C-ABI library on the CPU: it loads, exports every function that
+include/gdn_b200.h declares, and rejects bad arguments before touching CUDA.
+
+Every call here fails argument validation, which returns before any CUDA API
+call, so no GPU is needed (the pointers passed are never dereferenced).
+"""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from gdn_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "gdn_b200.h")
+
+# a fake, 256-byte aligned address that is never dereferenced (calls fail validation first)
+P = 1 << 20
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^GDN_API\s+[\w\s\*]+?\b(gdn_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_bound_functions():
+    assert declared_functions() == sorted(_lib.SIGNATURES)
+
+
+def test_every_declared_symbol_is_exported(gdn_lib):
+    for name in declared_functions():
+        assert hasattr(gdn_lib, name), name
+        assert isinstance(getattr(gdn_lib, name), ctypes._CFuncPtr)
+
+
+def test_only_declared_symbols_are_exported(gdn_lib):
+    out = os.popen(f"nm -D --defined-only {gdn_lib._name}").read()
+    exported = sorted(l.split()[-1] for l in out.splitlines() if " T " in l and "gdn_" in l)
+    assert exported == declared_functions()
+
+
+def test_library_has_no_cuda_runtime_dependency(gdn_lib):
+    deps = os.popen(f"ldd {gdn_lib._name}").read()
+    assert "libcudart" not in deps and "libtorch" not in deps
+
+
+def test_abi_version_and_errors(gdn_lib):
+    assert gdn_lib.gdn_abi_version() == _lib.ABI_VERSION
+    for code in (0, -1, -2, -3, -4, -5):
+        assert _lib.strerror(code)
+    assert "unknown" in _lib.strerror(-99)
+
+
+def decode_args(**over):
+    a = dict(q=P, k=P, v=P, state=P, A_log=P, a=P, dt_bias=P, b=P, scale=0.0, output=P,
+             new_state=P, B=1, H=16, HV=32, K=128, V=128, l2=0, stream=None)
+    a.update(over)
+    return list(a.values())
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(q=None), _lib.GDN_ERR_NULL),
+    (dict(state=None), _lib.GDN_ERR_NULL),
+    (dict(output=None), _lib.GDN_ERR_NULL),
+    (dict(new_state=None), _lib.GDN_ERR_NULL),
+    (dict(K=64), _lib.GDN_ERR_SHAPE),
+    (dict(V=256), _lib.GDN_ERR_SHAPE),
+    (dict(HV=33), _lib.GDN_ERR_SHAPE),
+    (dict(H=0), _lib.GDN_ERR_SHAPE),
+    (dict(B=-1), _lib.GDN_ERR_SHAPE),
+    (dict(B=1 << 20, HV=32), _lib.GDN_ERR_SHAPE),
+    (dict(state=P + 4), _lib.GDN_ERR_ALIGN),
+    (dict(new_state=P + 8), _lib.GDN_ERR_ALIGN),
+    (dict(q=P + 2), _lib.GDN_ERR_ALIGN),
+    (dict(v=P + 1), _lib.GDN_ERR_ALIGN),
+    (dict(A_log=P + 2), _lib.GDN_ERR_ALIGN),
+    (dict(new_state=P + 1024), _lib.GDN_ERR_ALIAS),
+])
+def test_decode_rejects_before_launch(gdn_lib, over, code):
+    assert gdn_lib.gdn_decode(*decode_args(**over)) == code
+
+
+def test_pooled_rejects(gdn_lib):
+    f = gdn_lib.gdn_decode_pooled
+    base = dict(q=P, k=P, v=P, pool=P, pool_size=4, idx=P, oidx=None, A_log=P, a=P, dt_bias=P,
+                b=P, scale=0.0, output=P, B=2, H=4, HV=8, K=128, V=128, l2=0, bad=None,
+                stream=None)
+
+    def call(**over):
+        d = dict(base)
+        d.update(over)
+        return f(*d.values())
+
+    assert call(idx=None) == _lib.GDN_ERR_NULL
+    assert call(pool_size=0) == _lib.GDN_ERR_SHAPE
+    assert call(idx=P + 2) == _lib.GDN_ERR_ALIGN
+    assert call(bad=P + 1) == _lib.GDN_ERR_ALIGN
+
+
+def test_mtp_rejects(gdn_lib):
+    f = gdn_lib.gdn_decode_mtp
+    base = dict(q=P, k=P, v=P, pool=P, pool_size=2, idx=None, A_log=P, a=P, dt_bias=P, b=P,
+                scale=0.0, output=P, inter=P, cache_steps=4, disable=0, B=2, T=4, H=4, HV=8,
+                K=128, V=128, l2=0, bad=None, stream=None)
+
+    def call(**over):
+        d = dict(base)
+        d.update(over)
+        return f(*d.values())
+
+    assert call(T=0) == _lib.GDN_ERR_SHAPE
+    assert call(cache_steps=3) == _lib.GDN_ERR_SHAPE           # intermediates shorter than T
+    assert call(pool_size=1) == _lib.GDN_ERR_SHAPE             # no indices: pool must hold B
+    assert call(inter=P + 4) == _lib.GDN_ERR_ALIGN
+    assert call(v=None) == _lib.GDN_ERR_NULL
+
+
+def test_tuned_rejects_unknown_shape_without_launch(gdn_lib):
+    f = gdn_lib.gdn_decode_tuned
+    args = [P, P, P, P, 2, None, P, P, P, P, 0.0, P, 2, 1, 4, 8, 128, 128, 0, 12, 1, 1, None]
+    assert f(*args) == _lib.GDN_ERR_SHAPE                       # 12 lanes per row
+    args[19] = 8
+    args[20] = 3
+    assert f(*args) == _lib.GDN_ERR_SHAPE                       # 3 rows per lane
+
+
+def test_interleave_rejects(gdn_lib):
+    f = gdn_lib.gdn_interleave_heads
+    assert f(None, P, 2, 4, 8, 128, None) == _lib.GDN_ERR_NULL
+    assert f(P, P * 2, 0, 4, 8, 128, None) == _lib.GDN_ERR_SHAPE
+    assert f(P, P * 2, 2, 4, 8, 126, None) == _lib.GDN_ERR_SHAPE
+    assert f(P + 4, P * 2, 2, 4, 8, 128, None) == _lib.GDN_ERR_ALIGN
+    assert f(P, P + 64, 2, 4, 8, 128, None) == _lib.GDN_ERR_ALIAS

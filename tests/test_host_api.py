@@ -1,0 +1,96 @@
+"""Host-side logic of the Python API on the CPU: argument checks (which run
+before any library call), the synthetic input recipe and the byte model."""
+
+import math
+
+import pytest
+import torch
+
+import gdn_b200
+from gdn_b200 import ops, synthetic
+
+
+def small(B=2, T=1, H=4, HV=8):
+    return synthetic.make_inputs(B=B, T=T, H=H, HV=HV, seed=3)
+
+
+def test_cpu_tensors_are_refused_no_fallback():
+    inp = small()
+    out = torch.empty(2, 1, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        gdn_b200.kernel_cuda_b200(*inp.args(), out, inp.state)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        gdn_b200.gdn_decode(*inp.args())
+
+
+def test_shape_and_dtype_checks():
+    inp = small()
+    with pytest.raises(TypeError, match="state must be torch.float32"):
+        ops._check(inp.state.half(), "state", torch.float32)
+    with pytest.raises(ValueError, match="head dims"):
+        ops._check_step_inputs(inp.q[..., :64], inp.k[..., :64], inp.v, inp.A_log, inp.a,
+                               inp.dt_bias, inp.b)
+    with pytest.raises(ValueError, match="multiple"):
+        ops._check_step_inputs(inp.q[:, :, :3], inp.k[:, :, :3], inp.v, inp.A_log, inp.a,
+                               inp.dt_bias, inp.b)
+    with pytest.raises(ValueError, match="expected T == 1"):
+        t2 = small(T=2)
+        ops._check_step_inputs(t2.q, t2.k, t2.v, t2.A_log, t2.a, t2.dt_bias, t2.b, T_expected=1)
+
+
+def test_pool_argument_rules():
+    inp = small()
+    args = inp.args()[:8]
+    f = gdn_b200.gated_delta_rule_decode_pretranspose
+    with pytest.raises(ValueError, match="together"):
+        f(*args, initial_state=inp.state)
+    with pytest.raises(ValueError, match="pool mode"):
+        f(*args, output_state_indices=torch.zeros(2, dtype=torch.int32))
+    with pytest.raises(ValueError, match="either state"):
+        f(*args[:3], None, *args[4:8])
+    with pytest.raises(ValueError, match="shape"):
+        ops._index_tensor(torch.zeros(3, dtype=torch.int32), "idx", 2, torch.device("cpu"))
+    with pytest.raises(TypeError, match="int32 or int64"):
+        ops._index_tensor(torch.zeros(2), "idx", 2, torch.device("cpu"))
+    idx = ops._index_tensor(torch.tensor([3, -1]), "idx", 2, torch.device("cpu"))
+    assert idx.dtype == torch.int32 and idx.tolist() == [3, -1]
+
+
+def test_scale_default():
+    assert ops._resolve_scale(None, 128) == 1 / math.sqrt(128)
+    assert ops._resolve_scale(0.0, 128) == 1 / math.sqrt(128)
+    assert ops._resolve_scale(0.5, 128) == 0.5
+
+
+def test_synthetic_inputs_are_seeded_and_distributed():
+    a = synthetic.make_inputs(B=4, seed=5)
+    b = synthetic.make_inputs(B=4, seed=5)
+    for x, y in zip(a.args()[:8], b.args()[:8]):
+        assert torch.equal(x, y)
+    assert a.q.shape == (4, 1, 16, 128) and a.v.shape == (4, 1, 32, 128)
+    assert a.state.shape == (4, 32, 128, 128) and a.state.dtype == torch.float32
+    assert a.q.dtype == torch.bfloat16 and a.a.shape == (4, 1, 32)
+    assert -2.0 <= float(a.A_log.min()) and float(a.A_log.max()) <= 1.0
+    assert abs(float(a.state.std()) - 0.1) < 0.01
+    assert a.scale == 1 / math.sqrt(128)
+
+
+def test_pool_indices_are_distinct_with_padding():
+    idx = synthetic.make_pool_indices(256, 1024, seed=0, n_pad=1)
+    assert idx.dtype == torch.int32 and idx.shape == (256,)
+    live = idx[idx >= 0]
+    assert (idx == -1).sum() == 1 and len(set(live.tolist())) == 255
+    assert int(live.max()) < 1024
+
+
+def test_byte_model():
+    # 131,844 bytes per (batch, v-head) update + 256 bytes of A_log/dt_bias per call
+    for B in (1, 8, 256):
+        assert synthetic.bytes_per_call(B) == 4_219_008 * B + 256
+    assert synthetic.bytes_per_call(256) == 1_080_066_304
+
+
+def test_registry_mirrors_reference_shape():
+    fns = gdn_b200.load_algo_functions()
+    assert set(fns) == set(gdn_b200.ALGO_ENTRY_POINTS)
+    assert gdn_b200.ALGO_NO_DPS <= set(fns)
