@@ -55,12 +55,21 @@ struct StepArgs {
   const int32_t* idx_out;   // [B] write slots, or null (= read slot)
   int32_t* bad_count;       // device counter of out-of-range indices, or null
   float scale;
-  int B, T, H, HV, hv_per_h;
+  int B, T, H, HV;
   int pool;                 // number of slots in state_in/state_out
   int cache_steps;
   int l2norm;
   int write_final;
+  uint32_t hv_mul, hv_shift;  // n / HV        as (umulhi(n, mul) + n) >> shift
+  uint32_t hq_mul, hq_shift;  // n / (HV / H)
 };
+
+// Division by a runtime divisor d >= 1 for 0 <= n < 2^31 with one multiply-high,
+// one add and one shift (round-up multiplier method, Granlund & Montgomery 1994):
+// shift = ceil(log2 d), mul = floor(2^32 * (2^shift - d) / d) + 1.
+__device__ __forceinline__ int div_fast(int n, uint32_t mul, uint32_t shift) {
+  return static_cast<int>((__umulhi(static_cast<uint32_t>(n), mul) + static_cast<uint32_t>(n)) >> shift);
+}
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
@@ -113,10 +122,35 @@ __device__ __forceinline__ void group_sum2(float& x, float& y, int lane) {
   y = hi ? keep : other;
 }
 
-// softplus with PyTorch's default threshold (x > 20 returns x), as in
-// solution/triton/kernel.py:74 (F.softplus) and :290.
-__device__ __forceinline__ float softplus_f(float x) {
-  return x > 20.0f ? x : log1pf(expf(x));
+// Gate math on the critical path of every warp, written in the log2 domain so
+// that it costs three hardware exp2/log2 approximations (ex2/lg2.approx, relative
+// error ~2^-22) instead of the longer accurate expf/log1pf sequences:
+//   softplus(x) * log2(e) = log2(1 + 2^(x log2 e))     (x if x > 20: PyTorch's
+//                                                      threshold, kernel.py:74, :290)
+//   g    = exp(-exp(A_log) * softplus(x)) = 2^(neg_exp_A * softplus(x) * log2 e)
+//   beta = 1 / (1 + 2^(-b log2 e))
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float log2_approx(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// -exp(A_log)
+__device__ __forceinline__ float neg_exp(float a_log) { return -exp2_approx(a_log * kLog2e); }
+// decay g from neg_exp_A = -exp(A_log) and x = a + dt_bias
+__device__ __forceinline__ float decay_gate(float neg_exp_A, float x) {
+  const float t = x * kLog2e;
+  const float sp2 = x > 20.0f ? t : log2_approx(1.0f + exp2_approx(t));
+  return exp2_approx(neg_exp_A * sp2);
+}
+__device__ __forceinline__ float update_gate(float b) {
+  return __frcp_rn(1.0f + exp2_approx(-b * kLog2e));
 }
 
 // Per-token inputs of one warp, kept packed until they are used so that the
@@ -149,9 +183,9 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   const int bh = blockIdx.x / kTPH;
   const int tile_in_head = blockIdx.x - bh * kTPH;
   const int row0 = tile_in_head * kRPC + warp * kRPW + grp;  // row of r is row0 + r*kGroups
-  const int bi = bh / p.HV;
+  const int bi = div_fast(bh, p.hv_mul, p.hv_shift);
   const int hv = bh - bi * p.HV;
-  const int hq = hv / p.hv_per_h;
+  const int hq = div_fast(hv, p.hq_mul, p.hq_shift);
   const int T = TT ? TT : p.T;
 
   // ---- slots -------------------------------------------------------------
@@ -207,7 +241,7 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
 
   TokenRaw<kNC, RG> cur;
   load_token(0, cur);
-  const float neg_exp_A = -expf(__ldg(p.A_log + hv));
+  const float neg_exp_A = neg_exp(__ldg(p.A_log + hv));
   const float dt_b = __ldg(p.dt_bias + hv);
 
   for (int t = 0; t < T; ++t) {
@@ -216,8 +250,8 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
 
     // Gates (solution/triton/kernel.py:73-75): g = exp(-exp(A_log)*softplus(a+dt_bias)),
     // beta = sigmoid(b).
-    const float g = expf(neg_exp_A * softplus_f(bf16_to_f32(cur.a) + dt_b));
-    const float beta = 1.0f / (1.0f + expf(-bf16_to_f32(cur.b)));
+    const float g = decay_gate(neg_exp_A, bf16_to_f32(cur.a) + dt_b);
+    const float beta = update_gate(bf16_to_f32(cur.b));
 
     float qf[kEPL], kf[kEPL];
 #pragma unroll
@@ -367,13 +401,24 @@ LaunchFn pick_launch(LaunchShape s) {
   return nullptr;
 }
 
-// Launch shape by regime.  Small batch is latency-bound: many small CTAs spread
-// the rows over all 148 SMs so each SM issues a few KB of loads at once.
-// Large batch is bandwidth-bound: bigger CTAs, two rows per lane.
+// Launch shape by regime, from CUPTI sweeps of all 36 shapes on B200 (16/32 heads):
+//  - T = 1: 4-warp CTAs of 4-row warps (8 lanes per row) are fastest or within
+//    1 % of the fastest at B = 1 (256 CTAs over 148 SMs, latency-bound), B = 64
+//    and B = 256 (bandwidth-bound); between 65 and 512 heads (B <= 16) warps of 16
+//    rows in 1-warp CTAs win (B = 8: 7.4 us vs 7.7 us);
+//  - T > 1: 16 rows per warp keep four independent rows per lane in flight across
+//    the token loop (B = 64, T = 2..4: best at 8/4/1, 8/1/4 is 1.9x slower).
 LaunchShape default_shape(long long heads, int T) {
-  if (T > 1) return LaunchShape{8, 1, 4};
-  if (heads <= 256) return LaunchShape{8, 1, 1};
-  return LaunchShape{8, 2, 4};
+  if (T > 1) return LaunchShape{8, 4, 1};
+  if (heads > 64 && heads <= 512) return LaunchShape{8, 4, 1};
+  return LaunchShape{8, 1, 4};
+}
+
+// Constants of div_fast for divisor d >= 1.
+void div_constants(uint32_t d, uint32_t& mul, uint32_t& shift) {
+  shift = 0;
+  while ((1ull << shift) < d) ++shift;
+  mul = static_cast<uint32_t>(((1ull << 32) * ((1ull << shift) - d)) / d + 1);
 }
 
 bool aligned(const void* ptr, size_t n) { return (reinterpret_cast<uintptr_t>(ptr) % n) == 0; }
@@ -387,15 +432,21 @@ float resolve_scale(double scale, int K) {
   return (scale == 0.0) ? static_cast<float>(1.0 / sqrt(static_cast<double>(K))) : static_cast<float>(scale);
 }
 
+// Returned by check_common when the sizes are valid and B == 0: the call is a
+// no-op (empty tensors may carry NULL pointers).
+constexpr int kNothingToDo = 1;
+
 int check_common(const void* q, const void* k, const void* v, const void* state, const void* A_log,
                  const void* a, const void* dt_bias, const void* b, const void* output, int B, int T,
                  int H, int HV, int K, int V, long long slots) {
-  if (!q || !k || !v || !state || !A_log || !a || !dt_bias || !b || !output) return GDN_ERR_NULL;
   if (K != kDim || V != kDim) return GDN_ERR_SHAPE;
-  if (B < 0 || T < 1 || H < 1 || HV < 1 || HV % H != 0 || slots < 1) return GDN_ERR_SHAPE;
+  if (B < 0 || T < 1 || H < 1 || HV < 1 || HV % H != 0) return GDN_ERR_SHAPE;
   // grid size and 32-bit index products stay in range
   if (static_cast<long long>(B) * HV * kDim > 0x7fffffffLL) return GDN_ERR_SHAPE;
   if (static_cast<long long>(B) * T * H > 0x7fffffffLL / kDim) return GDN_ERR_SHAPE;
+  if (B == 0) return kNothingToDo;
+  if (slots < 1) return GDN_ERR_SHAPE;
+  if (!q || !k || !v || !state || !A_log || !a || !dt_bias || !b || !output) return GDN_ERR_NULL;
   if (!aligned(state, 16) || !aligned(q, 8) || !aligned(k, 8) || !aligned(v, 2) ||
       !aligned(a, 2) || !aligned(b, 2) || !aligned(output, 2) || !aligned(A_log, 4) ||
       !aligned(dt_bias, 4))
@@ -430,11 +481,12 @@ StepArgs make_args(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, cons
   p.T = T;
   p.H = H;
   p.HV = HV;
-  p.hv_per_h = HV / H;
   p.pool = pool;
   p.cache_steps = T;
   p.l2norm = use_qk_l2norm ? 1 : 0;
   p.write_final = 1;
+  div_constants(static_cast<uint32_t>(HV), p.hv_mul, p.hv_shift);
+  div_constants(static_cast<uint32_t>(HV / H), p.hq_mul, p.hq_shift);
   return p;
 }
 
@@ -461,7 +513,8 @@ int gdn_decode(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const fl
                double scale, gdn_bf16* output, float* new_state, int B, int H, int HV, int K, int V,
                int use_qk_l2norm, void* stream) {
   const int rc = check_common(q, k, v, state, A_log, a, dt_bias, b, output, B, 1, H, HV, K, V,
-                              B > 0 ? B : 1);
+                              B);
+  if (rc == kNothingToDo) return GDN_OK;
   if (rc != GDN_OK) return rc;
   if (!new_state) return GDN_ERR_NULL;
   if (!aligned(new_state, 16)) return GDN_ERR_ALIGN;
@@ -481,6 +534,7 @@ int gdn_decode_pooled(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, f
                       int32_t* bad_index_count, void* stream) {
   const int rc = check_common(q, k, v, state_pool, A_log, a, dt_bias, b, output, B, 1, H, HV, K,
                               V, pool_size);
+  if (rc == kNothingToDo) return GDN_OK;
   if (rc != GDN_OK) return rc;
   if (!state_indices) return GDN_ERR_NULL;
   if (!aligned(state_indices, 4) || !aligned(output_state_indices, 4) ||
@@ -503,6 +557,7 @@ int gdn_decode_mtp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, floa
                    int use_qk_l2norm, int32_t* bad_index_count, void* stream) {
   const int rc = check_common(q, k, v, state_pool, A_log, a, dt_bias, b, output, B, T, H, HV, K,
                               V, pool_size);
+  if (rc == kNothingToDo) return GDN_OK;
   if (rc != GDN_OK) return rc;
   if (!state_indices && pool_size < B) return GDN_ERR_SHAPE;
   if (intermediate_states && cache_steps < T) return GDN_ERR_SHAPE;
@@ -531,6 +586,7 @@ int gdn_decode_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, fl
                      void* stream) {
   const int rc = check_common(q, k, v, state_pool, A_log, a, dt_bias, b, output, B, T, H, HV, K,
                               V, pool_size);
+  if (rc == kNothingToDo) return GDN_OK;
   if (rc != GDN_OK) return rc;
   if (!state_indices && pool_size < B) return GDN_ERR_SHAPE;
   if (!aligned(state_indices, 4)) return GDN_ERR_ALIGN;

@@ -23,6 +23,8 @@ LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200.so")
 
 SOURCES = ["gdn_decode.cu"]
+TVM_LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200_tvm.so")
+TVM_SOURCES = ["tvm_ffi_entry.cu", "gdn_decode.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo",
@@ -76,6 +78,45 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB_PATH
 
 
+def _tvm_ffi_paths():
+    """(include dirs, library dir) of the installed tvm_ffi package, or None."""
+    try:
+        from tvm_ffi import libinfo
+    except ImportError:
+        return None
+    incs = [libinfo.find_include_path(), libinfo.find_dlpack_include_path()]
+    return incs, os.path.dirname(libinfo.find_libtvm_ffi())
+
+
+def build_tvm_ffi(force: bool = False) -> str | None:
+    """Compile libgdn_b200_tvm.so: the decode step exported as the TVM-FFI function
+    ``kernel_cuda_b200``, the reference's native boundary.  Skipped (None) when
+    tvm_ffi is not installed."""
+    paths = _tvm_ffi_paths()
+    if paths is None:
+        return None
+    incs, libdir = paths
+    deps = [os.path.join(SRC_DIR, s) for s in TVM_SOURCES] + _deps()
+    if (not force and os.path.exists(TVM_LIB_PATH)
+            and all(os.path.getmtime(d) <= os.path.getmtime(TVM_LIB_PATH) for d in deps)):
+        return TVM_LIB_PATH
+    os.makedirs(LIB_DIR, exist_ok=True)
+    tmp = TVM_LIB_PATH + ".tmp"
+    cmd = [_nvcc(), *NVCC_FLAGS, "-I", INCLUDE_DIR]
+    for inc in incs:
+        cmd += ["-I", inc]
+    cmd += ["-o", tmp, *[os.path.join(SRC_DIR, s) for s in TVM_SOURCES],
+            f"-L{libdir}", "-ltvm_ffi", "-Xlinker", f"-rpath={libdir}"]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(
+            "nvcc failed (%d):\n%s\n%s" % (proc.returncode, " ".join(cmd), proc.stderr[-8000:])
+        )
+    os.replace(tmp, TVM_LIB_PATH)
+    return TVM_LIB_PATH
+
+
 if __name__ == "__main__":
-    path = build(force="--force" in sys.argv, verbose="-v" in sys.argv)
-    print(path)
+    force = "--force" in sys.argv
+    print(build(force=force, verbose="-v" in sys.argv))
+    print(build_tvm_ffi(force=force))

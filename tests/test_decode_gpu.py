@@ -143,20 +143,37 @@ def test_full_size_b256_sampled_heads():
     check(out[sel.to(DEV)], g.state[sel.to(DEV)], *want)
 
 
-def test_repeated_steps_track_oracle():
-    """Eight decode steps in a row on the same state (a decode loop)."""
+@pytest.mark.parametrize("l2", [True, False])
+def test_repeated_steps_track_oracle(l2):
+    """Several decode steps in a row on the same state (a decode loop).
+
+    With L2-normalised q/k (the model's setting) the state stays bounded and the
+    fixed tolerances hold over 8 steps.  With raw N(0,1) keys (|k|^2 ~ 128) each
+    step scales the state along k by about |1 - beta |k|^2|, amplifying fp32
+    rounding by the same factor, so 3 steps are checked with tolerances scaled
+    to the largest state and output magnitude."""
+    steps = 8 if l2 else 3
     inp = synthetic.make_inputs(B=4, seed=21)
     g = inp.to(DEV)
     S = inp.state.clone()
-    for step in range(8):
+    outs, want_outs = [], []
+    for step in range(steps):
         nxt = synthetic.make_inputs(B=4, seed=1000 + step)
         o_ref, S = gdn_ref.decode(nxt.q, nxt.k, nxt.v, S, inp.A_log, nxt.a, inp.dt_bias, nxt.b,
-                                  inp.scale)
+                                  inp.scale, use_qk_l2norm=l2)
         gn = nxt.to(DEV)
         out, _ = gdn_b200.gdn_decode(gn.q, gn.k, gn.v, g.state, g.A_log, gn.a, g.dt_bias, gn.b,
-                                     g.scale)
-        torch.testing.assert_close(out.float().cpu(), o_ref.float(), **OUT_TOL)
-    torch.testing.assert_close(g.state.cpu(), S, **STATE_TOL)
+                                     g.scale, use_qk_l2norm=l2)
+        outs.append(out.float().cpu())
+        want_outs.append(o_ref.float())
+    if l2:
+        for o, w in zip(outs, want_outs):
+            torch.testing.assert_close(o, w, **OUT_TOL)
+        torch.testing.assert_close(g.state.cpu(), S, **STATE_TOL)
+    else:
+        for o, w in zip(outs, want_outs):
+            torch.testing.assert_close(o, w, rtol=1e-2, atol=1e-2 * float(w.abs().max()))
+        torch.testing.assert_close(g.state.cpu(), S, rtol=1e-3, atol=1e-3 * float(S.abs().max()))
 
 
 def test_bad_arguments_raise_on_gpu():
