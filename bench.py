@@ -46,6 +46,8 @@ for _p in (PKG_ROOT, ROOT):
 
 import torch  # noqa: E402
 
+from gdn_b200.timing import cupti_kernel_durations_us, l2_flush_buffer  # noqa: E402
+
 METRIC = "GDN decode µs (CUPTI) at B=1; state-update HBM GB/s vs peak at B=256"
 UNIT = "GB/s"
 BATCH, H, HV, DIM = 256, 16, 32, 128
@@ -255,29 +257,6 @@ def workload_config(world):
     }
 
 
-def l2_flush_buffer(device):
-    return torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
-
-
-def cupti_kernel_durations_us(fn, iters, device, name="gdn_step_kernel", flush=None):
-    """Median-ready list of device durations (us) of kernels whose name contains
-    ``name``, from CUPTI activity records (torch.profiler); ``flush`` runs before
-    every launch to empty the L2."""
-    from torch.profiler import ProfilerActivity, profile
-
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        for _ in range(iters):
-            if flush is not None:
-                flush()
-            fn()
-        torch.cuda.synchronize(device)
-    out = []
-    for e in prof.profiler.kineto_results.events():
-        if name in e.name() and str(e.device_type()).endswith("CUDA"):
-            out.append(e.duration_ns() / 1e3)
-    return out
-
-
 def b1_latency(device, iters=200):
     import gdn_b200
     from gdn_b200 import synthetic
@@ -293,6 +272,11 @@ def b1_latency(device, iters=200):
         fn()
     d = cupti_kernel_durations_us(fn, iters, device, flush=flush_buf.zero_)
     d_warm = cupti_kernel_durations_us(fn, iters, device, flush=None)
+    # floor of the method: the same 2 MiB state read and written in place by a plain
+    # elementwise kernel (torch mul_), same flush, same CUPTI records
+    scratch = inp.state.clone()
+    floor = cupti_kernel_durations_us(lambda: scratch.mul_(1.0), iters, device,
+                                      name="MulFunctor", flush=flush_buf.zero_)
     res = {"median_us": None, "source": "cupti (torch.profiler activity records)",
            "l2": "flushed before every launch (256 MiB write)", "iters": len(d)}
     if d:
@@ -301,6 +285,9 @@ def b1_latency(device, iters=200):
                    p90_us=round(d[(9 * len(d)) // 10], 3))
     if d_warm:
         res["median_us_l2_warm"] = round(statistics.median(d_warm), 3)
+    if floor:
+        res["copy_floor_us"] = round(statistics.median(floor), 3)
+        res["copy_floor"] = "torch in-place mul_ of the same 2 MiB state, L2 flushed, CUPTI"
     return res
 
 

@@ -164,8 +164,12 @@ struct TokenRaw {
 };
 
 // One kernel body for every variant of the step:
-//   TT == 1: single token (decode), TT == 0: T tokens from p.T (multi-token).
-template <int LPR, int RG, int W, int TT>
+//   TT == 1: single token (decode), TT == 0: T tokens from p.T (multi-token);
+//   POOL: slots come from p.idx_in / p.idx_out; L2N: q and k are L2-normalised.
+// The flags are compile-time so that the plain decode path carries no code for
+// the variants it does not use (at small batch instruction fetch after a cold
+// start is part of the critical path).
+template <int LPR, int RG, int W, int TT, bool POOL, bool L2N>
 __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   constexpr int kGroups = 32 / LPR;     // row groups per warp
   constexpr int kRPW = kGroups * RG;    // rows per warp
@@ -193,7 +197,7 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   int slot_out = bi;
   bool active = true;
   bool do_write = p.write_final != 0;
-  if (p.idx_in != nullptr) {
+  if constexpr (POOL) {
     slot_in = __ldg(p.idx_in + bi);
     const bool counted = (hv == 0 && tile_in_head == 0 && threadIdx.x == 0);
     if (slot_in < 0 || slot_in >= p.pool) {
@@ -223,8 +227,9 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
       for (int c = 0; c < kNC; ++c) h[r][c] = ld_state(src + r * kGroups * kDim + c * LPR * 4);
   }
 
+  // Offsets into q/k/v/a/b/output fit in 31 bits (checked on the host).
   auto load_token = [&](int t, TokenRaw<kNC, RG>& raw) {
-    const size_t bt = static_cast<size_t>(bi) * T + t;
+    const int bt = bi * T + t;
     const uint2* qp = reinterpret_cast<const uint2*>(p.q + (bt * p.H + hq) * kDim + gl * 4);
     const uint2* kp = reinterpret_cast<const uint2*>(p.k + (bt * p.H + hq) * kDim + gl * 4);
 #pragma unroll
@@ -268,7 +273,7 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
     float qk = 0.0f;
 #pragma unroll
     for (int e = 0; e < kEPL; ++e) qk = fmaf(qf[e], kf[e], qk);
-    if (p.l2norm) {
+    if constexpr (L2N) {
       // x * rsqrt(sum(x^2) + 1e-6), the convention of
       // flashinfer/gdn_kernels/gdn_decode_pretranspose.py:253-254.
       float qq = 0.0f, kk = 0.0f;
@@ -294,11 +299,8 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
     } else {
       qk = group_sum<LPR>(qk);
     }
-#pragma unroll
-    for (int e = 0; e < kEPL; ++e) qf[e] *= p.scale;
-    qk *= p.scale;
 
-    const size_t bt = static_cast<size_t>(bi) * T + t;
+    const int bt = bi * T + t;
     uint16_t* op = p.out + (bt * p.HV + hv) * kDim + row0;
     if (active) {
 #pragma unroll
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
         float qh = qh0 + qh1;
         group_sum2<LPR>(kh, qh, lane);
         const float dv = beta * (bf16_to_f32(cur.v[r]) - g * kh);
-        const float o = fmaf(g, qh, dv * qk);
+        const float o = p.scale * fmaf(g, qh, dv * qk);
 #pragma unroll
         for (int c = 0; c < kNC; ++c) {
           h[r][c].x = fmaf(dv, kf[4 * c + 0], g * h[r][c].x);
@@ -376,29 +378,43 @@ struct LaunchShape {
   int lpr, rg, warps;
 };
 
-template <int LPR, int RG, int W, int TT>
+template <int LPR, int RG, int W, int TT, bool POOL, bool L2N>
 cudaError_t launch_step(const StepArgs& p, cudaStream_t stream) {
   constexpr int kRPC = (32 / LPR) * RG * W;
   const long long ctas = static_cast<long long>(p.B) * p.HV * (kDim / kRPC);
-  gdn_step_kernel<LPR, RG, W, TT><<<static_cast<unsigned>(ctas), W * 32, 0, stream>>>(p);
+  gdn_step_kernel<LPR, RG, W, TT, POOL, L2N>
+      <<<static_cast<unsigned>(ctas), W * 32, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
 using LaunchFn = cudaError_t (*)(const StepArgs&, cudaStream_t);
 
-template <int TT>
+// Every launch shape is instantiated for the plain path (tuning sweeps); the pooled
+// and L2-normalised paths carry the shapes the default heuristic can choose.
+template <int TT, bool POOL, bool L2N>
 LaunchFn pick_launch(LaunchShape s) {
 #define GDN_SHAPE(L, R, W) \
-  if (s.lpr == L && s.rg == R && s.warps == W) return &launch_step<L, R, W, TT>;
+  if (s.lpr == L && s.rg == R && s.warps == W) return &launch_step<L, R, W, TT, POOL, L2N>;
 #define GDN_SHAPES_W(L, R) GDN_SHAPE(L, R, 1) GDN_SHAPE(L, R, 2) GDN_SHAPE(L, R, 4) GDN_SHAPE(L, R, 8)
 #define GDN_SHAPES_R(L) GDN_SHAPES_W(L, 1) GDN_SHAPES_W(L, 2) GDN_SHAPES_W(L, 4)
-  GDN_SHAPES_R(8)
-  GDN_SHAPES_R(16)
-  GDN_SHAPES_R(32)
+  if constexpr (!POOL && !L2N) {
+    GDN_SHAPES_R(8)
+    GDN_SHAPES_R(16)
+    GDN_SHAPES_R(32)
+  } else {
+    GDN_SHAPE(8, 1, 4)
+    GDN_SHAPE(8, 4, 1)
+  }
 #undef GDN_SHAPES_R
 #undef GDN_SHAPES_W
 #undef GDN_SHAPE
   return nullptr;
+}
+
+template <int TT>
+LaunchFn pick_variant(LaunchShape s, bool pool, bool l2n) {
+  if (pool) return l2n ? pick_launch<TT, true, true>(s) : pick_launch<TT, true, false>(s);
+  return l2n ? pick_launch<TT, false, true>(s) : pick_launch<TT, false, false>(s);
 }
 
 // Launch shape by regime, from CUPTI sweeps of all 36 shapes on B200 (16/32 heads):
@@ -444,6 +460,7 @@ int check_common(const void* q, const void* k, const void* v, const void* state,
   // grid size and 32-bit index products stay in range
   if (static_cast<long long>(B) * HV * kDim > 0x7fffffffLL) return GDN_ERR_SHAPE;
   if (static_cast<long long>(B) * T * H > 0x7fffffffLL / kDim) return GDN_ERR_SHAPE;
+  if (static_cast<long long>(B) * T * HV > 0x7fffffffLL / kDim) return GDN_ERR_SHAPE;
   if (B == 0) return kNothingToDo;
   if (slots < 1) return GDN_ERR_SHAPE;
   if (!q || !k || !v || !state || !A_log || !a || !dt_bias || !b || !output) return GDN_ERR_NULL;
@@ -456,7 +473,8 @@ int check_common(const void* q, const void* k, const void* v, const void* state,
 
 int run(const StepArgs& p, LaunchShape shape, int TT, cudaStream_t stream) {
   if (p.B == 0) return GDN_OK;
-  LaunchFn fn = (TT == 1) ? pick_launch<1>(shape) : pick_launch<0>(shape);
+  const bool pool = p.idx_in != nullptr, l2n = p.l2norm != 0;
+  LaunchFn fn = (TT == 1) ? pick_variant<1>(shape, pool, l2n) : pick_variant<0>(shape, pool, l2n);
   if (!fn) return GDN_ERR_SHAPE;
   return fn(p, stream) == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }

@@ -1,0 +1,41 @@
+"""Device-time measurement used by the benchmark and the comparison tests.
+
+Kernel durations come from CUPTI activity records through torch.profiler — the
+GPU-side start/end of each launch, without host launch overhead — which is the
+method the reference quotes its microsecond numbers with
+(flashinfer.testing.bench_gpu_time(enable_cupti=True, cold_l2_cache=True),
+scripts/bench_fi_timing.py:43-48).  A cold L2 is made the same way: a buffer
+larger than the 126 MB L2 is zeroed before every launch.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, List, Optional
+
+import torch
+
+L2_FLUSH_BYTES = 256 * 1024 * 1024
+
+
+def l2_flush_buffer(device) -> torch.Tensor:
+    return torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+
+
+def cupti_kernel_durations_us(fn: Callable[[], object], iters: int, device,
+                              name: str = "gdn_step_kernel",
+                              flush: Optional[Callable[[], object]] = None) -> List[float]:
+    """Device durations (µs) of the kernels whose name contains ``name`` over
+    ``iters`` calls of ``fn``; ``flush`` runs before every call."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(iters):
+            if flush is not None:
+                flush()
+            fn()
+        torch.cuda.synchronize(device)
+    out = []
+    for e in prof.profiler.kineto_results.events():
+        if name in e.name() and str(e.device_type()).endswith("CUDA"):
+            out.append(e.duration_ns() / 1e3)
+    return out

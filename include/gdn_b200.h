@@ -147,7 +147,9 @@ GDN_API int gdn_decode_mtp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16*
  * state_indices, or gdn_decode in place when state_indices is NULL), with
  * an explicit work split: lanes_per_row in {8,16,32} lanes share one 512-byte
  * state row, rows_per_lane in {1,2,4}, warps_per_cta in {1,2,4,8}; 0 keeps
- * the library's default for that field.  Used by the benchmark's sweeps.
+ * the library's default for that field.  With state_indices or use_qk_l2norm
+ * only the default shapes (8/1/4 and 8/4/1) are built; any other shape returns
+ * GDN_ERR_SHAPE.  Used by the benchmark's sweeps.
  */
 GDN_API int gdn_decode_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
                      float* state_pool, int pool_size,
