@@ -21,6 +21,9 @@ roofline        the decode kernel alone (CUDA events around each launch).
 cpu_baseline    the reference's CPU algorithm (oracle restatement of
         kernel_pt_reference, its per-head loop) on a bounded sample, host cores.
 
+At N > 1 the output exchange is fused into the decode kernel (each rank stores its
+rows into every rank's buffer over NVLink, then a bounded barrier); ``--tp-collective
+nccl`` uses NCCL all-gather + the interleave kernel instead.
 ``--impl reference`` times that CPU implementation alone as the reference arm.
 ``--sweep PATH`` also writes a batch sweep (B in 1..256, plus the pooled and
 multi-token configurations) as JSON to PATH.
@@ -333,17 +336,24 @@ def run_b200_arm(args, rank, world, local_rank):
     # local shard inputs, drawn on the device
     inp = synthetic.make_inputs(B=BATCH, H=hl, HV=hvl, seed=1234 + rank, device=device)
     out = torch.empty((BATCH, 1, HV, DIM), dtype=torch.bfloat16, device=device)
-    tp = TPDecode(H=H, HV=HV, max_batch=BATCH, device=device) if world > 1 else None
+    tp = (TPDecode(H=H, HV=HV, max_batch=BATCH, device=device, collective=args.tp_collective)
+          if world > 1 else None)
+
+    # N > 1: the step (decode + exchange) is captured once as CUDA graphs and
+    # replayed, so host-side Python does not bound the ~20-80 us per-rank step.
+    graphs = tp.capture(*inp.args()) if tp is not None else None
 
     def step(events=None):
-        if tp is not None:
-            return tp.step(*inp.args(), out=out, kernel_events=events)
         if events is not None:
             events[0].record()
-        gdn_b200.kernel_cuda_b200(*inp.args(), out, inp.state)
+        if graphs is not None:
+            res = graphs.replay()
+        else:
+            gdn_b200.kernel_cuda_b200(*inp.args(), out, inp.state)
+            res = out
         if events is not None:
             events[1].record()
-        return out
+        return res
 
     parity = parity_check(inp.args(), device, step, shard)
     for _ in range(args.warmup):
@@ -387,8 +397,8 @@ def run_b200_arm(args, rank, world, local_rank):
     def e2e_step():
         for n, t in host.items():
             getattr(inp, n).copy_(t, non_blocking=True)
-        step()
-        out_host.copy_(out, non_blocking=True)
+        res = step()
+        out_host.copy_(res, non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -420,8 +430,10 @@ def run_b200_arm(args, rank, world, local_rank):
                          "(oracle restatement of kernel_pt_reference's per-head loop, torch CPU fp32)"}
 
     if world > 1:
+        if tp.collective == "peer":
+            tp.check()
         torch.distributed.barrier()
-        del tp
+        del graphs, tp
         torch.distributed.destroy_process_group()
     if rank != 0:
         return
@@ -429,6 +441,7 @@ def run_b200_arm(args, rank, world, local_rank):
     peaks = load_peaks()
     achieved = local_bytes / (kernel_ms / 1e3) / 1e9
     traffic = ncu_traffic_per_launch() if world == 1 else None
+    # N>1: decode + barrier kernels (peer) or decode + interleave kernels (NCCL)
     launches_per_step = 1 if world == 1 else 2
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
@@ -444,7 +457,12 @@ def run_b200_arm(args, rank, world, local_rank):
                      "algorithmic_bytes_per_launch": local_bytes},
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": K_e2e, "api": "gdn_b200.kernel_cuda_b200"
-                if world == 1 else "gdn_b200.tp.TPDecode.step"},
+                if world == 1 else "gdn_b200.tp.TPDecode.capture(...).replay()"},
+        "tp_exchange": None if world == 1 else (
+            "fused: decode kernel stores outputs into every rank's buffer over NVLink, "
+            "then a one-CTA barrier kernel (roofline.kernel_us covers both); CUDA graphs"
+            if args.tp_collective == "peer" else
+            "NCCL all_gather_into_tensor + interleave kernel; CUDA graphs"),
         "gpu_launches": launches_per_step * K,
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -518,6 +536,8 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--skip-b1", action="store_true", help="omit the B=1 latency leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--tp-collective", choices=["peer", "nccl"], default="peer",
+                    help="output exchange at N > 1: fused peer stores (default) or NCCL")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

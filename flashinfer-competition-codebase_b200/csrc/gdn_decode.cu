@@ -38,6 +38,7 @@ namespace {
 
 constexpr int kDim = 128;                // K == V == 128 on this path
 constexpr int kHeadElems = kDim * kDim;  // fp32 elements of one head's state
+constexpr int kMaxRanks = 8;             // GPUs of one NVLink node
 
 struct StepArgs {
   const uint16_t* q;        // [B, T, H, K]  bf16
@@ -62,6 +63,19 @@ struct StepArgs {
   int write_final;
   uint32_t hv_mul, hv_shift;  // n / HV        as (umulhi(n, mul) + n) >> shift
   uint32_t hq_mul, hq_shift;  // n / (HV / H)
+  // Tensor-parallel output scatter (SCATTER kernels only).  This rank owns v-heads
+  // [hv0, hv0 + HV) of hv_total; its outputs go to every rank's output buffer.
+  uint16_t* peer_out[kMaxRanks];  // [B, hv_total, V] bf16 of each rank, mapped here
+  int world, hv0, hv_total;
+};
+
+// Arguments of the cross-rank barrier that completes a tensor-parallel step.
+struct BarrierArgs {
+  uint32_t* peer_sig[kMaxRanks];  // [world] signal words of each rank, mapped here
+  uint32_t* epoch;                // this rank's count of completed barriers (device)
+  int32_t* status;                // set to 1 if a wait timed out
+  unsigned long long timeout_ns;
+  int rank, world;
 };
 
 // Division by a runtime divisor d >= 1 for 0 <= n < 2^31 with one multiply-high,
@@ -95,6 +109,21 @@ __device__ __forceinline__ void st_state(float* ptr, const float4& x) {
   asm volatile("st.global.cs.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "f"(x.x), "f"(x.y),
                "f"(x.z), "f"(x.w)
                : "memory");
+}
+
+// Cross-GPU signalling over NVLink peer memory (system scope).
+__device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
 template <int LPR>
@@ -169,7 +198,10 @@ struct TokenRaw {
 // The flags are compile-time so that the plain decode path carries no code for
 // the variants it does not use (at small batch instruction fetch after a cold
 // start is part of the critical path).
-template <int LPR, int RG, int W, int TT, bool POOL, bool L2N>
+//   SCATTER (T = 1, no pool): tensor-parallel step; the CTA's output rows are
+//   staged in shared memory and stored into every rank's output buffer over
+//   NVLink, then the ranks meet at a bounded barrier (see the epilogue).
+template <int LPR, int RG, int W, int TT, bool POOL, bool L2N, bool SCATTER>
 __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   constexpr int kGroups = 32 / LPR;     // row groups per warp
   constexpr int kRPW = kGroups * RG;    // rows per warp
@@ -178,6 +210,9 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   constexpr int kNC = kEPL / 4;         // 16-byte chunks per lane per row
   constexpr int kTPH = kDim / kRPC;     // CTAs per head
   static_assert(kDim % kRPC == 0, "rows per CTA must divide V");
+  static_assert(!SCATTER || (TT == 1 && !POOL && kRPC % 8 == 0),
+                "the scatter epilogue moves whole 16-byte chunks of T=1 outputs");
+  __shared__ __align__(16) uint16_t s_out[SCATTER ? kRPC : 1];
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -329,7 +364,13 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
           h[r][c].z = fmaf(dv, kf[4 * c + 2], g * h[r][c].z);
           h[r][c].w = fmaf(dv, kf[4 * c + 3], g * h[r][c].w);
         }
-        if (gl == 0) op[r * kGroups] = f32_to_bf16(o);
+        if (gl == 0) {
+          if constexpr (SCATTER) {
+            s_out[warp * kRPW + r * kGroups + grp] = f32_to_bf16(o);
+          } else {
+            op[r * kGroups] = f32_to_bf16(o);
+          }
+        }
       }
       if (TT != 1 && p.inter != nullptr) {
         float* ip = p.inter + ((static_cast<size_t>(bi) * p.cache_steps + t) * p.HV + hv) * kHeadElems +
@@ -354,6 +395,55 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
 #pragma unroll
       for (int c = 0; c < kNC; ++c) st_state(dst + r * kGroups * kDim + c * LPR * 4, h[r][c]);
   }
+
+  if constexpr (SCATTER) {
+    // The CTA's kRPC outputs (one head, rows tile_in_head*kRPC ...) go to every
+    // rank's output buffer as 16-byte NVLink stores, overlapping the other CTAs'
+    // math.  Completion is established by tp_barrier_kernel, which runs after this
+    // grid has finished (all of its stores performed).
+    constexpr int kChunks = kRPC * 2 / 16;
+    __syncthreads();
+    if (threadIdx.x < p.world * kChunks) {
+      const int peer = threadIdx.x / kChunks;
+      const int c = threadIdx.x - peer * kChunks;
+      uint4* dst = reinterpret_cast<uint4*>(
+          p.peer_out[peer] + (static_cast<size_t>(bi) * p.hv_total + p.hv0 + hv) * kDim +
+          tile_in_head * kRPC);
+      dst[c] = reinterpret_cast<const uint4*>(s_out)[c];
+    }
+  }
+}
+
+// Cross-rank barrier of a tensor-parallel step, one thread per rank j: announce to
+// rank j that this rank's outputs are in place (system-scope release of the step's
+// epoch into word `rank` of j's signal array), then wait until rank j has announced
+// the same in this rank's array (acquire).  The epoch is this rank's device counter
+// of completed barriers plus one (every rank runs the same sequence of barriers, so
+// the values agree), advanced here after the waits: the kernel takes no per-call
+// value and can be replayed from a CUDA graph.  The stream runs it after the decode
+// grid, whose completion makes that grid's peer stores visible.  Each wait is
+// bounded: past timeout_ns it records the failure in *status and gives up.
+__global__ void tp_barrier_kernel(const BarrierArgs p) {
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) s_epoch = *p.epoch + 1u;
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int j = threadIdx.x;
+  if (j < p.world) {
+    __threadfence_system();
+    st_release_sys(p.peer_sig[j] + p.rank, e);
+    const uint32_t* mine = p.peer_sig[p.rank] + j;
+    const unsigned long long t0 = global_ns();
+    while (static_cast<int>(ld_acquire_sys(mine) - e) < 0) {
+      if (global_ns() - t0 > p.timeout_ns) {
+        atomicOr(p.status, 1);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *p.epoch = e;
 }
 
 // Tensor-parallel head interleave: gathered [W, rows, HVl, V] -> out [rows, W*HVl, V],
@@ -378,16 +468,26 @@ struct LaunchShape {
   int lpr, rg, warps;
 };
 
-template <int LPR, int RG, int W, int TT, bool POOL, bool L2N>
+using LaunchFn = cudaError_t (*)(const StepArgs&, cudaStream_t);
+
+template <int LPR, int RG, int W, int TT, bool POOL, bool L2N, bool SCATTER = false>
 cudaError_t launch_step(const StepArgs& p, cudaStream_t stream) {
   constexpr int kRPC = (32 / LPR) * RG * W;
   const long long ctas = static_cast<long long>(p.B) * p.HV * (kDim / kRPC);
-  gdn_step_kernel<LPR, RG, W, TT, POOL, L2N>
+  gdn_step_kernel<LPR, RG, W, TT, POOL, L2N, SCATTER>
       <<<static_cast<unsigned>(ctas), W * 32, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
-using LaunchFn = cudaError_t (*)(const StepArgs&, cudaStream_t);
+// Tensor-parallel (scatter) kernels exist for the two default T=1 shapes.
+LaunchFn pick_scatter(LaunchShape s, bool l2n) {
+  if (s.lpr == 8 && s.rg == 1 && s.warps == 4)
+    return l2n ? &launch_step<8, 1, 4, 1, false, true, true> : &launch_step<8, 1, 4, 1, false, false, true>;
+  if (s.lpr == 8 && s.rg == 4 && s.warps == 1)
+    return l2n ? &launch_step<8, 4, 1, 1, false, true, true> : &launch_step<8, 4, 1, 1, false, false, true>;
+  return nullptr;
+}
+
 
 // Every launch shape is instantiated for the plain path (tuning sweeps); the pooled
 // and L2-normalised paths carry the shapes the default heuristic can choose.
@@ -522,6 +622,7 @@ const char* gdn_strerror(int code) {
     case GDN_ERR_ALIGN: return "misaligned pointer (state needs 16 B, q/k 8 B, fp32 vectors 4 B, bf16 2 B)";
     case GDN_ERR_LAUNCH: return "CUDA kernel launch failed";
     case GDN_ERR_ALIAS: return "state and new_state overlap without being the same buffer";
+    case GDN_ERR_ARG: return "invalid argument value (rank or world out of range)";
     default: return "unknown gdn error code";
   }
 }
@@ -616,6 +717,46 @@ int gdn_decode_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, fl
   if (rows_per_lane > 0) s.rg = rows_per_lane;
   if (warps_per_cta > 0) s.warps = warps_per_cta;
   return run(p, s, T == 1 ? 1 : 0, static_cast<cudaStream_t>(stream));
+}
+
+int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float* state,
+                  const float* A_log, const gdn_bf16* a, const float* dt_bias, const gdn_bf16* b,
+                  double scale, gdn_bf16* const* peer_outputs, uint32_t* const* peer_signals,
+                  uint32_t* epoch_counter, int32_t* status, uint32_t timeout_us, int rank,
+                  int world, int B, int H, int HV, int K, int V, int use_qk_l2norm,
+                  void* stream) {
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return GDN_ERR_ARG;
+  if (static_cast<long long>(HV) * world > 0x7fffffffLL / kDim) return GDN_ERR_SHAPE;
+  const int rc = check_common(q, k, v, state, A_log, a, dt_bias, b, peer_outputs, B, 1, H,
+                              HV * world, K, V, B);
+  if (rc == kNothingToDo) return GDN_OK;
+  if (rc != GDN_OK) return rc;
+  if (!peer_signals || !status || !epoch_counter) return GDN_ERR_NULL;
+  if (!aligned(status, 4) || !aligned(epoch_counter, 4)) return GDN_ERR_ALIGN;
+  StepArgs p = make_args(q, k, v, state, state, A_log, a, dt_bias, b, scale, nullptr, B, 1, H, HV,
+                         K, B, use_qk_l2norm);
+  BarrierArgs bar{};
+  for (int r = 0; r < world; ++r) {
+    if (!peer_outputs[r] || !peer_signals[r]) return GDN_ERR_NULL;
+    if (!aligned(peer_outputs[r], 16) || !aligned(peer_signals[r], 4)) return GDN_ERR_ALIGN;
+    p.peer_out[r] = peer_outputs[r];
+    bar.peer_sig[r] = peer_signals[r];
+  }
+  p.out = peer_outputs[rank];
+  p.world = world;
+  p.hv0 = rank * HV;
+  p.hv_total = HV * world;
+  bar.status = status;
+  bar.epoch = epoch_counter;
+  bar.timeout_ns = 1000ull * (timeout_us ? timeout_us : 1000000u);
+  bar.rank = rank;
+  bar.world = world;
+  LaunchFn fn = pick_scatter(default_shape(static_cast<long long>(B) * HV, 1), p.l2norm != 0);
+  if (!fn) return GDN_ERR_SHAPE;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (fn(p, st) != cudaSuccess) return GDN_ERR_LAUNCH;
+  tp_barrier_kernel<<<1, 32, 0, st>>>(bar);
+  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
 int gdn_interleave_heads(const gdn_bf16* gathered, gdn_bf16* output, int world, int rows, int HVl,

@@ -16,6 +16,7 @@ from .build import LIB_PATH
 _P = ctypes.c_void_p
 _I = ctypes.c_int
 _D = ctypes.c_double
+_U = ctypes.c_uint32
 
 # Every function declared in include/gdn_b200.h with its ctypes signature.
 SIGNATURES = {
@@ -36,6 +37,11 @@ SIGNATURES = {
         [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _D, _P,
          _I, _I, _I, _I, _I, _I, _I, _I, _I, _I, _P],
     ),
+    "gdn_decode_tp": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _P, _U,
+         _I, _I, _I, _I, _I, _I, _I, _I, _P],
+    ),
     "gdn_interleave_heads": (_I, [_P, _P, _I, _I, _I, _I, _P]),
 }
 
@@ -47,6 +53,7 @@ GDN_ERR_SHAPE = -2
 GDN_ERR_ALIGN = -3
 GDN_ERR_LAUNCH = -4
 GDN_ERR_ALIAS = -5
+GDN_ERR_ARG = -6
 
 
 class GdnError(RuntimeError):

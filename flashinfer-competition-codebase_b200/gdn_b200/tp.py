@@ -4,22 +4,32 @@ Every (batch entry, v-head) update is independent, so rank r of W owns a
 contiguous block of HV/W v-heads together with the H/W q/k heads they read
 (v-head hv reads q/k head hv // (HV/H), so a contiguous split keeps each
 pair on one rank), the matching slices of A_log, dt_bias, a and b, and its
-own state [B, HV/W, V, K].  The state update needs no communication.  The
-one exchange is the output: each rank's bf16 [B, T, HV/W, V] is all-gathered
-over NVLink by NCCL into a rank-major buffer [W, B*T, HV/W, V], which the
-library's head-interleave kernel turns into [B, T, HV, V].
+own state [B, HV/W, V, K].  The state update needs no communication; the one
+exchange is the output, which every rank needs in full ([B, 1, HV, V]).
+
+Two ways to do that exchange:
+
+* ``collective="peer"`` (default on GPUs): the decode kernel of each rank
+  stores each output row straight into every rank's output buffer over NVLink
+  while the other rows are still being computed, then a one-CTA kernel makes
+  the ranks meet at a bounded barrier on signal words (``gdn_decode_tp``).  The buffers are torch symmetric memory with NVLink
+  multicast disabled (plain peer pointers only); outputs alternate between two
+  buffers by step parity so a fast rank cannot overwrite rows a slow rank is
+  still reading.
+* ``collective="nccl"``: the local kernel writes [B, 1, HV/W, V], NCCL
+  all-gathers it into a rank-major buffer [W, B, HV/W, V], and the library's
+  head-interleave kernel reorders it.  This is the baseline, and the path the
+  CPU (gloo) tests exercise with stand-in per-rank steps.
 
 The reference runs on one GPU only; this layer has no counterpart there.  The
 head split corresponds to the contest definition itself, which is Qwen3-Next's
 16/32 heads split four ways (4 q/k, 8 v-heads per rank).
-
-Collectives go through ``torch.distributed`` on the given group (NCCL on
-GPUs, gloo in the CPU tests, where the per-rank step and the interleave are
-supplied by the test).
 """
 
 from __future__ import annotations
 
+import ctypes
+import os
 from typing import Callable, Optional
 
 import torch
@@ -74,17 +84,18 @@ def _cuda_interleave(gathered, out):
 
 
 class TPDecode:
-    """One decode step per call on this rank's head shard, outputs all-gathered.
+    """One decode step per call on this rank's head shard, outputs exchanged.
 
-    Buffers for the local output and the gathered outputs are allocated once
-    for ``max_batch`` entries and reused.  ``local_step(q, k, v, state, A_log,
-    a, dt_bias, b, scale, out)`` and ``interleave(gathered, out)`` default to
-    the CUDA kernels; tests on CPU ranks pass stand-ins.
+    Buffers are allocated once for ``max_batch`` entries and reused.  With
+    ``collective="nccl"``, ``local_step(q, k, v, state, A_log, a, dt_bias, b,
+    scale, out)`` and ``interleave(gathered, out)`` default to the CUDA kernels;
+    tests on CPU ranks pass stand-ins.
     """
 
     def __init__(self, H: int, HV: int, max_batch: int, V: int = 128,
                  group: Optional[dist.ProcessGroup] = None, device=None,
-                 local_step: Optional[Callable] = None, interleave: Optional[Callable] = None):
+                 local_step: Optional[Callable] = None, interleave: Optional[Callable] = None,
+                 collective: Optional[str] = None, timeout_us: int = 1_000_000):
         self.group = group
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
@@ -92,22 +103,127 @@ class TPDecode:
         self.V = V
         self.max_batch = max_batch
         self.device = torch.device(device) if device is not None else torch.device("cuda")
+        if collective is None:
+            collective = "peer" if (self.device.type == "cuda" and local_step is None) else "nccl"
+        if collective not in ("peer", "nccl"):
+            raise ValueError(f"collective must be 'peer' or 'nccl', got {collective!r}")
+        self.collective = collective
+        self.timeout_us = int(timeout_us)
+        self._steps = 0              # host count of peer steps: output buffer parity
         n = max_batch * self.shard.hv_local * V
-        self._local = torch.empty(n, dtype=torch.bfloat16, device=self.device)
-        self._gathered = torch.empty(world * n, dtype=torch.bfloat16, device=self.device)
-        self.local_step = local_step or _cuda_local_step
-        self.interleave = interleave or _cuda_interleave
+        if collective == "nccl":
+            self._local = torch.empty(n, dtype=torch.bfloat16, device=self.device)
+            self._gathered = torch.empty(world * n, dtype=torch.bfloat16, device=self.device)
+            self.local_step = local_step or _cuda_local_step
+            self.interleave = interleave or _cuda_interleave
+        else:
+            if local_step is not None or interleave is not None:
+                raise ValueError("stand-in steps apply to collective='nccl' only")
+            self._init_peer()
+
+    # -- peer-memory exchange --------------------------------------------------
+    def _init_peer(self):
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        import torch.distributed._symmetric_memory as symm_mem
+
+        W = self.shard.world
+        self._out_bytes = self.max_batch * self.shard.HV * self.V * 2
+        self._sig_off = 2 * self._out_bytes
+        total = self._sig_off + 256
+        group = self.group if self.group is not None else dist.group.WORLD
+        self._buf = symm_mem.empty(total, dtype=torch.uint8, device=self.device)
+        self._buf[self._sig_off:].zero_()
+        self._hdl = symm_mem.rendezvous(self._buf, group)
+        ptrs = [int(x) for x in self._hdl.buffer_ptrs]
+        if len(ptrs) != W:
+            raise RuntimeError(f"symmetric memory mapped {len(ptrs)} ranks, expected {W}")
+        P = ctypes.c_void_p
+        self._peer_out = [(P * W)(*[x + k * self._out_bytes for x in ptrs]) for k in (0, 1)]
+        self._peer_sig = (P * W)(*[x + self._sig_off for x in ptrs])
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._epoch = torch.zeros(1, dtype=torch.int32, device=self.device)  # device counter
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+
+    def _peer_step(self, q, k, v, state, A_log, a, dt_bias, b, scale, B, events, parity=None):
+        from . import _lib
+        from .ops import _check, _check_step_inputs, _resolve_scale
+
+        Bq, T, Hl, HVl, K, V, dev = _check_step_inputs(q, k, v, A_log, a, dt_bias, b, T_expected=1)
+        if Hl != self.shard.h_local or HVl != self.shard.hv_local:
+            raise ValueError("inputs are not this rank's head shard")
+        _check(state, "state", torch.float32, (B, HVl, V, K), dev)
+        if parity is None:
+            parity = self._steps & 1
+            self._steps += 1
+        e0, e1 = events if events is not None else (None, None)
+        if e0 is not None:
+            e0.record()
+        with torch.cuda.device(dev):
+            _lib.call(
+                "gdn_decode_tp", q.data_ptr(), k.data_ptr(), v.data_ptr(), state.data_ptr(),
+                A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
+                _resolve_scale(scale, K), self._peer_out[parity], self._peer_sig,
+                self._epoch.data_ptr(), self.status.data_ptr(), self.timeout_us,
+                self.shard.rank, self.shard.world, B, Hl, HVl, K, V, 0,
+                torch.cuda.current_stream(dev).cuda_stream)
+        if e1 is not None:
+            e1.record()
+        return self._peer_view(B, parity)
+
+    def _peer_view(self, B, parity):
+        start = parity * self._out_bytes
+        nbytes = B * self.shard.HV * self.V * 2
+        return self._buf[start:start + nbytes].view(torch.bfloat16).view(B, 1, self.shard.HV, self.V)
+
+    @torch.no_grad()
+    def capture(self, q, k, v, state, A_log, a, dt_bias, b, scale) -> "CapturedSteps":
+        """Record this rank's step on these (fixed) input tensors as CUDA graphs.
+
+        Replaying a graph runs the step on whatever the tensors hold at that time,
+        with no host work besides the graph launch.  The peer exchange alternates
+        two output buffers, so two graphs are recorded (one per buffer) and
+        ``CapturedSteps.replay`` alternates them; every rank must replay the same
+        number of steps.  Nothing is executed while capturing."""
+        B = q.shape[0]
+        graphs, outs = [], []
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        for parity in (0, 1):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                if self.collective == "peer":
+                    out = self._peer_step(q, k, v, state, A_log, a, dt_bias, b, scale, B, None,
+                                          parity=parity)
+                else:
+                    out = self.step(q, k, v, state, A_log, a, dt_bias, b, scale)
+            graphs.append(g)
+            outs.append(out)
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        return CapturedSteps(self, graphs, outs)
+    def check(self) -> None:
+        """Raise if a cross-rank wait of the peer exchange has timed out (syncs)."""
+        if self.collective == "peer" and int(self.status.item()) != 0:
+            raise RuntimeError("gdn_decode_tp: a rank did not reach the output barrier in time")
 
     @torch.no_grad()
     def step(self, q, k, v, state, A_log, a, dt_bias, b, scale, out=None,
              kernel_events=None) -> torch.Tensor:
         """Inputs are this rank's shards (``HeadShard.shard_inputs``); the local
-        state is updated in place.  Returns the full output [B, 1, HV, V].
-        ``kernel_events`` = (start, end) CUDA events recorded around the local
-        decode launch, for timing it apart from the all-gather."""
+        state is updated in place.  Returns the full output [B, 1, HV, V]: with
+        ``collective="peer"`` and ``out=None`` that is a view of an internal
+        buffer, valid until the next-but-one step (pass ``out`` to get a copy).
+        ``kernel_events`` = (start, end) CUDA events recorded around the decode
+        launch (for ``"peer"`` the launch includes the exchange)."""
         B = q.shape[0]
         if B > self.max_batch:
             raise ValueError(f"batch {B} exceeds max_batch {self.max_batch}")
+        if self.collective == "peer":
+            res = self._peer_step(q, k, v, state, A_log, a, dt_bias, b, scale, B, kernel_events)
+            if out is not None:
+                out.copy_(res)
+                return out
+            return res
         W, hvl, V = self.shard.world, self.shard.hv_local, self.V
         if out is None:
             out = torch.empty((B, 1, self.shard.HV, V), dtype=torch.bfloat16, device=self.device)
@@ -128,3 +244,21 @@ class TPDecode:
         dist.all_gather_into_tensor(gathered, self._local[:n], group=self.group)
         self.interleave(gathered.view(W, B, hvl, V), out.view(B, self.shard.HV, V))
         return out
+
+
+class CapturedSteps:
+    """Two recorded TP steps (see ``TPDecode.capture``), replayed alternately."""
+
+    def __init__(self, tp: TPDecode, graphs, outs):
+        self.tp, self.graphs, self.outs = tp, graphs, outs
+        self.count = 0
+
+    def replay(self) -> torch.Tensor:
+        """Run one step; returns its output [B, 1, HV, V] (valid until the
+        next-but-one replay)."""
+        i = self.count & 1
+        self.graphs[i].replay()
+        self.count += 1
+        if self.tp.collective == "peer":
+            self.tp._steps += 1
+        return self.outs[i]

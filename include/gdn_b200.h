@@ -55,6 +55,7 @@ typedef uint16_t gdn_bf16;
 #define GDN_ERR_ALIGN (-3)       /* a pointer is not suitably aligned     */
 #define GDN_ERR_LAUNCH (-4)      /* the CUDA launch failed                */
 #define GDN_ERR_ALIAS (-5)       /* in/out buffers overlap illegally      */
+#define GDN_ERR_ARG (-6)         /* invalid argument value                */
 
 #define GDN_ABI_VERSION 1
 
@@ -159,6 +160,44 @@ GDN_API int gdn_decode_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf1
                      gdn_bf16* output, int B, int T, int H, int HV, int K,
                      int V, int use_qk_l2norm, int lanes_per_row,
                      int rows_per_lane, int warps_per_cta, void* stream);
+
+/*
+ * Tensor-parallel T=1 decode step with the output all-gather fused in.
+ *
+ * No counterpart in the reference (it runs on one GPU; its qk4/v8 contest shape
+ * is itself a 4-way head split of Qwen3-Next).  Rank `rank` of `world` (<= 8)
+ * holds H q/k heads, HV v-heads (v-heads [rank*HV, (rank+1)*HV) of world*HV),
+ * their A_log/dt_bias/a/b and its own state [B, HV, V, K], updated in place.
+ * The decode kernel stores each output row straight into every rank's output
+ * buffer peer_outputs[r] ([B, 1, world*HV, V] bf16, rank r's buffer mapped into
+ * this process, e.g. by CUDA IPC or symmetric memory) at this rank's head
+ * offset, overlapping the NVLink traffic with the math; a one-CTA barrier
+ * kernel enqueued after it then synchronises the ranks through signal words:
+ * peer_signals[r] points to `world` uint32 words on rank r (zero before the
+ * first call); this rank writes the step's epoch into word `rank` of every
+ * rank's array and waits until all `world` words of its own array reach it.
+ * When the barrier kernel has finished, peer_outputs[rank] holds all
+ * world*HV heads.
+ *  - epoch_counter: one uint32 in this GPU's memory, zero before the first
+ *    call; the barrier kernel reads it, uses value+1 as the step's epoch and
+ *    stores that back (wrapping past 2^32 is handled).  Because no per-call
+ *    value is passed, the two kernels can be captured in a CUDA graph and
+ *    replayed.
+ *  - status: int32 in device memory; set to 1 (never cleared by the library)
+ *    if the wait for some rank exceeded timeout_us (0 = 1 s); the barrier then
+ *    returns instead of waiting forever, and that output is incomplete.
+ *  - Two consecutive calls must not write the same output buffers (a fast rank
+ *    could overwrite rows a slow rank is still reading): alternate two buffers.
+ * Every rank must make the same sequence of calls with the same B, H, HV and
+ * world.  Enqueues two kernels on `stream`.
+ */
+GDN_API int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                          float* state, const float* A_log, const gdn_bf16* a,
+                          const float* dt_bias, const gdn_bf16* b, double scale,
+                          gdn_bf16* const* peer_outputs, uint32_t* const* peer_signals,
+                          uint32_t* epoch_counter, int32_t* status, uint32_t timeout_us,
+                          int rank, int world, int B, int H, int HV, int K, int V,
+                          int use_qk_l2norm, void* stream);
 
 /*
  * Head interleave after a tensor-parallel output all-gather.

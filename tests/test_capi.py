@@ -133,3 +133,27 @@ def test_interleave_rejects(gdn_lib):
     assert f(P, P * 2, 2, 4, 8, 126, None) == _lib.GDN_ERR_SHAPE
     assert f(P + 4, P * 2, 2, 4, 8, 128, None) == _lib.GDN_ERR_ALIGN
     assert f(P, P + 64, 2, 4, 8, 128, None) == _lib.GDN_ERR_ALIAS
+
+
+def test_tp_rejects(gdn_lib):
+    import ctypes
+    f = gdn_lib.gdn_decode_tp
+    arr = (ctypes.c_void_p * 2)(P, P)
+    base = dict(q=P, k=P, v=P, state=P, A_log=P, a=P, dt_bias=P, b=P, scale=0.0, outs=arr,
+                sigs=arr, epoch=P, status=P, timeout=0, rank=0, world=2, B=2, H=8,
+                HV=16, K=128, V=128, l2=0, stream=None)
+
+    def call(**over):
+        d = dict(base)
+        d.update(over)
+        return f(*d.values())
+
+    assert call(world=9) == _lib.GDN_ERR_ARG
+    assert call(rank=2) == _lib.GDN_ERR_ARG
+    assert call(epoch=None) == _lib.GDN_ERR_NULL
+    assert call(epoch=P + 2) == _lib.GDN_ERR_ALIGN
+    assert call(sigs=None) == _lib.GDN_ERR_NULL
+    assert call(status=None) == _lib.GDN_ERR_NULL
+    assert call(outs=(ctypes.c_void_p * 2)(P, None)) == _lib.GDN_ERR_NULL
+    assert call(outs=(ctypes.c_void_p * 2)(P, P + 8)) == _lib.GDN_ERR_ALIGN
+    assert call(K=64) == _lib.GDN_ERR_SHAPE

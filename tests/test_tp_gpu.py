@@ -12,8 +12,10 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
+import ctypes
+
 import gdn_b200
-from gdn_b200 import synthetic
+from gdn_b200 import _lib, synthetic
 
 pytestmark = pytest.mark.gpu
 
@@ -36,7 +38,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, results):
+def _rank(rank, world, port, results, collective="peer", steps=2):
     for p in (PKG, ROOT):
         if p not in sys.path:
             sys.path.insert(0, p)
@@ -51,14 +53,16 @@ def _rank(rank, world, port, results):
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                                 timeout=timedelta(seconds=60))
         inp = syn.make_inputs(B=12, seed=90)                     # same full inputs on every rank
-        tp = TPDecode(H=16, HV=32, max_batch=16, device=dev)
+        tp = TPDecode(H=16, HV=32, max_batch=16, device=dev, collective=collective)
         local = [t.to(dev) for t in tp.shard.shard_inputs(inp.q, inp.k, inp.v, inp.state,
                                                           inp.A_log, inp.a, inp.dt_bias, inp.b)]
         outs = []
-        for _ in range(2):                                       # two steps on the local state
+        for _ in range(steps):                                   # steps on the local state
             outs.append(tp.step(*local, inp.scale).cpu())
         torch.cuda.synchronize(dev)
-        results[rank] = ("ok", outs[0], outs[1], local[3].cpu(), tp.shard.hv0, tp.shard.hv1)
+        if collective == "peer":
+            tp.check()
+        results[rank] = ("ok", outs, local[3].cpu(), tp.shard.hv0, tp.shard.hv1)
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:
@@ -66,17 +70,22 @@ def _rank(rank, world, port, results):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp_two_ranks_match_single_gpu():
-    world = 2
+@pytest.mark.parametrize("collective", ["peer", "nccl"])
+def test_tp_two_ranks_match_single_gpu(collective):
+    world, steps = 2, 3
     inp = synthetic.make_inputs(B=12, seed=90)
     g = inp.to("cuda:0")
-    o1, _ = gdn_b200.gdn_decode(*g.args())
-    o2, state2 = gdn_b200.gdn_decode(g.q, g.k, g.v, g.state, g.A_log, g.a, g.dt_bias, g.b, g.scale)
+    want = []
+    for _ in range(steps):
+        o, state = gdn_b200.gdn_decode(g.q, g.k, g.v, g.state, g.A_log, g.a, g.dt_bias, g.b,
+                                       g.scale)
+        want.append(o.cpu())
     ctx = mp.get_context("spawn")
     with ctx.Manager() as mgr:
         res = mgr.dict()
         port = _free_port()
-        procs = [ctx.Process(target=_rank, args=(r, world, port, res)) for r in range(world)]
+        procs = [ctx.Process(target=_rank, args=(r, world, port, res, collective, steps))
+                 for r in range(world)]
         for p in procs:
             p.start()
         for p in procs:
@@ -87,10 +96,91 @@ def test_tp_two_ranks_match_single_gpu():
         res = dict(res)
     for r in range(world):
         assert res[r][0] == "ok", res[r]
-        _, a, b, st, hv0, hv1 = res[r]
-        torch.testing.assert_close(a.float(), o1.float().cpu(), atol=1e-2, rtol=1e-2)
-        torch.testing.assert_close(b.float(), o2.float().cpu(), atol=1e-2, rtol=1e-2)
-        torch.testing.assert_close(st, state2[:, hv0:hv1].cpu(), atol=1e-3, rtol=1e-3)
+        _, outs, st, hv0, hv1 = res[r]
+        for got, w in zip(outs, want):
+            torch.testing.assert_close(got.float(), w.float(), atol=1e-2, rtol=1e-2)
+        torch.testing.assert_close(st, state[:, hv0:hv1].cpu(), atol=1e-3, rtol=1e-3)
+
+
+def _tp_call(g, out_ptrs, sig_ptrs, epoch, status, rank, world, timeout_us=0):
+    P = ctypes.c_void_p
+    B, _, H, K = g.q.shape
+    HV = g.v.shape[2]
+    _lib.call("gdn_decode_tp", g.q.data_ptr(), g.k.data_ptr(), g.v.data_ptr(), g.state.data_ptr(),
+              g.A_log.data_ptr(), g.a.data_ptr(), g.dt_bias.data_ptr(), g.b.data_ptr(), g.scale,
+              (P * world)(*out_ptrs), (P * world)(*sig_ptrs), epoch.data_ptr(),
+              status.data_ptr(), timeout_us, rank, world, B, H, HV, K, 128, 0,
+              torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("B", [1, 5, 64])
+def test_fused_step_single_rank_matches_plain_kernel(B):
+    """world = 1: scatter to the own buffer and a barrier with itself, over
+    several epochs alternating two output buffers."""
+    inp = synthetic.make_inputs(B=B, seed=95)
+    g, h = inp.to("cuda"), inp.to("cuda")
+    outs = [torch.full((B, 1, 32, 128), float("nan"), dtype=torch.bfloat16, device="cuda")
+            for _ in range(2)]
+    sig = torch.zeros(8, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    epoch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for step in range(1, 4):
+        out = outs[step & 1]
+        _tp_call(g, [out.data_ptr()], [sig.data_ptr()], epoch, status, 0, 1)
+        want, _ = gdn_b200.gdn_decode(*h.args())
+        torch.cuda.synchronize()
+        assert torch.equal(out, want) and torch.equal(g.state, h.state)
+    assert int(status.item()) == 0 and int(sig[0].item()) == 3 and int(epoch.item()) == 3
+
+
+def test_fused_step_replays_from_cuda_graphs():
+    """world = 1 through TPDecode.capture: the barrier's epoch lives on the device,
+    so replayed graphs keep advancing it; outputs alternate between two buffers."""
+    import torch.distributed as dist
+    from gdn_b200.tp import TPDecode
+
+    if dist.is_initialized():
+        pytest.skip("a process group is already initialised")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()),
+                      TORCH_SYMM_MEM_DISABLE_MULTICAST="1")
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda:0"))
+    try:
+        inp = synthetic.make_inputs(B=6, seed=97)
+        g, h = inp.to("cuda"), inp.to("cuda")
+        tp = TPDecode(H=16, HV=32, max_batch=8, device="cuda", collective="peer")
+        steps = tp.capture(*g.args())
+        for i in range(5):
+            out = steps.replay()
+            want, _ = gdn_b200.gdn_decode(*h.args())
+            torch.cuda.synchronize()
+            assert torch.equal(out, want) and torch.equal(g.state, h.state), i
+        assert int(tp._epoch.item()) == 5 and int(tp.status.item()) == 0
+        del steps
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_step_barrier_times_out_without_a_peer():
+    """Failure detection without a GPU fault: world = 2 with no second rank, so the
+    barrier word of rank 1 is never written.  The kernel gives up after the time
+    limit, records it in the status word and returns; the GPU stays usable."""
+    inp = synthetic.make_inputs(B=2, H=8, HV=16, seed=96)
+    g = inp.to("cuda")
+    out0 = torch.zeros((2, 1, 32, 128), dtype=torch.bfloat16, device="cuda")
+    out1 = torch.zeros_like(out0)
+    sig0 = torch.zeros(8, dtype=torch.int32, device="cuda")
+    sig1 = torch.zeros(8, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    epoch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _tp_call(g, [out0.data_ptr(), out1.data_ptr()], [sig0.data_ptr(), sig1.data_ptr()],
+             epoch, status, 0, 2, timeout_us=20000)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 1
+    assert int(sig1[0].item()) == 1 and int(sig0[0].item()) == 1 and int(sig0[1].item()) == 0
+    # rank 0's 16 heads reached both buffers; rank 1's half is untouched
+    assert torch.equal(out0[:, :, :16], out1[:, :, :16]) and torch.all(out0[:, :, 16:] == 0)
+    # the context is still healthy
+    test_fused_step_single_rank_matches_plain_kernel(1)
 
 
 def test_tp_world_one_is_the_plain_step():
