@@ -32,6 +32,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "../../include/gdn_b200.h"
 
 namespace {
@@ -623,6 +625,7 @@ const char* gdn_strerror(int code) {
     case GDN_ERR_LAUNCH: return "CUDA kernel launch failed";
     case GDN_ERR_ALIAS: return "state and new_state overlap without being the same buffer";
     case GDN_ERR_ARG: return "invalid argument value (rank or world out of range)";
+    case GDN_ERR_LIMIT: return "beyond the fixed scratch of gdn_decode_tp_static (channel must be 0..63)";
     default: return "unknown gdn error code";
   }
 }
@@ -757,6 +760,67 @@ int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float
   if (fn(p, st) != cudaSuccess) return GDN_ERR_LAUNCH;
   tp_barrier_kernel<<<1, 32, 0, st>>>(bar);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+}  // extern "C"
+
+// ---- allocation-free tensor-parallel step --------------------------------------
+//
+// Callers that cannot allocate device memory where they run a decode step (a
+// serving runtime that reserves all of HBM for its own pool at start-up, code that
+// runs while a CUDA graph is being captured, a plain-C host with no allocator of its
+// own) still have to give gdn_decode_tp an epoch counter.  gdn_decode_tp_static
+// keeps those counters in a fixed array inside this library instead: one uint32 per
+// "channel", kStaticChannels channels, resident on every GPU that loads the library
+// until the process exits.
+namespace {
+
+constexpr int kStaticChannels = 64;
+constexpr int kMaxDevices = 64;
+
+// Epoch counters of gdn_decode_tp_static, one per channel (zero when the library is
+// loaded).  Host code only ever sees a stand-in for this name: its device address
+// comes from cudaGetSymbolAddress, per device.
+static __device__ __align__(256) uint32_t g_tp_static_epochs[kStaticChannels];
+
+std::mutex g_static_mutex;
+uint32_t* g_static_epochs_dev[kMaxDevices];  // device address per device, null until set up
+
+// Device address of g_tp_static_epochs on the current device, looked up (with that
+// device current) on the first call for the device.
+int static_epochs(uint32_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_LAUNCH;
+  if (dev < 0 || dev >= kMaxDevices) return GDN_ERR_LIMIT;
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (g_static_epochs_dev[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_tp_static_epochs) != cudaSuccess) return GDN_ERR_LAUNCH;
+    g_static_epochs_dev[dev] = static_cast<uint32_t*>(ptr);
+  }
+  *out = g_static_epochs_dev[dev];
+  return GDN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gdn_decode_tp_static(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float* state,
+                         const float* A_log, const gdn_bf16* a, const float* dt_bias,
+                         const gdn_bf16* b, double scale, gdn_bf16* const* peer_outputs,
+                         uint32_t* const* peer_signals, int32_t* status, uint32_t timeout_us,
+                         int channel, int rank, int world, int B, int H, int HV, int K, int V,
+                         int use_qk_l2norm, void* stream) {
+  if (channel < 0 || channel >= kStaticChannels) return GDN_ERR_LIMIT;
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return GDN_ERR_ARG;
+  if (!peer_outputs || !peer_signals || !status) return GDN_ERR_NULL;
+  uint32_t* epochs = nullptr;
+  const int rc = static_epochs(&epochs);
+  if (rc != GDN_OK) return rc;
+  return gdn_decode_tp(q, k, v, state, A_log, a, dt_bias, b, scale, peer_outputs, peer_signals,
+                       epochs + channel, status, timeout_us, rank, world, B, H, HV, K, V,
+                       use_qk_l2norm, stream);
 }
 
 int gdn_interleave_heads(const gdn_bf16* gathered, gdn_bf16* output, int world, int rows, int HVl,

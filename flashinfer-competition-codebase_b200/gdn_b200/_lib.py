@@ -42,6 +42,11 @@ SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _P, _U,
          _I, _I, _I, _I, _I, _I, _I, _I, _P],
     ),
+    "gdn_decode_tp_static": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _U,
+         _I, _I, _I, _I, _I, _I, _I, _I, _I, _P],
+    ),
     "gdn_interleave_heads": (_I, [_P, _P, _I, _I, _I, _I, _P]),
 }
 
@@ -54,6 +59,7 @@ GDN_ERR_ALIGN = -3
 GDN_ERR_LAUNCH = -4
 GDN_ERR_ALIAS = -5
 GDN_ERR_ARG = -6
+GDN_ERR_LIMIT = -7
 
 
 class GdnError(RuntimeError):

@@ -56,6 +56,7 @@ typedef uint16_t gdn_bf16;
 #define GDN_ERR_LAUNCH (-4)      /* the CUDA launch failed                */
 #define GDN_ERR_ALIAS (-5)       /* in/out buffers overlap illegally      */
 #define GDN_ERR_ARG (-6)         /* invalid argument value                */
+#define GDN_ERR_LIMIT (-7)       /* beyond a fixed, built-in maximum      */
 
 #define GDN_ABI_VERSION 1
 
@@ -198,6 +199,38 @@ GDN_API int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* 
                           uint32_t* epoch_counter, int32_t* status, uint32_t timeout_us,
                           int rank, int world, int B, int H, int HV, int K, int V,
                           int use_qk_l2norm, void* stream);
+
+/*
+ * Allocation-free variant of gdn_decode_tp.  No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory where they run the decode
+ * step: a serving runtime that reserves all of HBM for its own pool at
+ * start-up, code that runs while a CUDA graph is being captured (cudaMalloc is
+ * not allowed there), a plain-C host without an allocator of its own.  The one
+ * piece of scratch gdn_decode_tp needs besides the caller's inputs, outputs and
+ * signal words is its epoch counter; here it comes from a fixed array inside
+ * the library: 64 uint32 "channels" (GDN_ERR_LIMIT outside 0..63), present on
+ * every GPU that loads the library until the process exits.  Nothing is
+ * allocated: no cudaMalloc, no cudaFree, no allocating library call.
+ *  - The first call on a device looks up the array's device address with that
+ *    device current (cudaGetSymbolAddress, checked); make that first call
+ *    before any stream capture on the device.
+ *  - A channel starts at zero when the library is loaded and keeps counting
+ *    across calls (the barrier's epoch continues; nothing is cleared per
+ *    call).  Use a channel with one set of signal words only (zero before its
+ *    first call on that channel), and the same channel number on every rank.
+ *  - Every call on a channel shares its counter: calls on the same channel
+ *    that overlap on the GPU (different streams, no ordering) race.
+ * Other arguments and results as gdn_decode_tp.
+ */
+GDN_API int gdn_decode_tp_static(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                                 float* state, const float* A_log, const gdn_bf16* a,
+                                 const float* dt_bias, const gdn_bf16* b, double scale,
+                                 gdn_bf16* const* peer_outputs,
+                                 uint32_t* const* peer_signals, int32_t* status,
+                                 uint32_t timeout_us, int channel, int rank, int world,
+                                 int B, int H, int HV, int K, int V, int use_qk_l2norm,
+                                 void* stream);
 
 /*
  * Head interleave after a tensor-parallel output all-gather.
