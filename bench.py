@@ -94,67 +94,108 @@ def ncu_traffic_per_launch():
 
 
 class ClockSampler:
-    """Samples SM clock, power and clock-event reasons of one GPU via NVML in a
-    background thread (every ~2 ms) while the timed region runs."""
+    """Samples SM clock, power and clock-event reasons while the timed region runs.
 
-    def __init__(self, device_index: int):
-        self.samples = []
-        self._stop = threading.Event()
+    ``mode="smi"``: an ``nvidia-smi --query-gpu ... -lms`` subprocess (a separate
+    process, so sampling cannot contend with this process's launches);
+    ``mode="nvml"``: a background thread polling NVML; ``mode="none"``: off.
+    Only one rank samples, for all GPUs of the node in use."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active")
+
+    def __init__(self, device_indices, mode: str = "nvml", interval_ms: int = 2):
+        self.mode = mode
+        self.indices = list(device_indices)
+        self.interval_ms = interval_ms
+        self.samples = []           # (sm_mhz, reasons_mask, power_w)
+        self.max_mhz = None
+        self._proc = None
         self._thread = None
-        self.ok = False
-        try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            self._nv = pynvml
+        self._stop = threading.Event()
+        if mode == "nvml":
             try:
-                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
-                self._h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
-            except Exception:
-                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self._reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
-            self.ok = True
-        except Exception as e:  # clocks are reported as unavailable
-            log(f"[bench] NVML unavailable: {e}")
-            self.max_mhz = None
+                import pynvml
 
-    def _run(self):
+                pynvml.nvmlInit()
+                self._nv = pynvml
+                self._h = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in self.indices]
+                self._reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) \
+                    or getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+                self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h[0], pynvml.NVML_CLOCK_SM)
+            except Exception as e:
+                log(f"[bench] NVML unavailable: {e}")
+                self.mode = "none"
+
+    def _run_nvml(self):
         nv = self._nv
         while not self._stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
-                rs = self._reasons(self._h)
-                pw = nv.nvmlDeviceGetPowerUsage(self._h) / 1000.0
-                self.samples.append((sm, rs, pw))
-            except Exception:
-                pass
-            time.sleep(0.002)
+            for h in self._h:
+                try:
+                    self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                         self._reasons(h), nv.nvmlDeviceGetPowerUsage(h) / 1e3))
+                except Exception:
+                    pass
+            time.sleep(self.interval_ms / 1e3)
 
     def start(self):
-        if self.ok:
-            self._thread = threading.Thread(target=self._run, daemon=True)
+        if self.mode == "nvml":
+            self._thread = threading.Thread(target=self._run_nvml, daemon=True)
             self._thread.start()
+        elif self.mode == "smi":
+            import subprocess
+
+            try:
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                     f"-lms={self.interval_ms}", "-i", ",".join(map(str, self.indices))],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                time.sleep(0.05)
+            except OSError as e:
+                log(f"[bench] nvidia-smi unavailable: {e}")
+                self.mode = "none"
 
     def stop(self):
         if self._thread is not None:
             self._stop.set()
             self._thread.join()
+        if self._proc is not None:
+            time.sleep(self.interval_ms / 1e3)
+            self._proc.terminate()
+            text, _ = self._proc.communicate(timeout=10)
+            for line in text.splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                try:
+                    self.samples.append((float(parts[1]), int(parts[4], 16), float(parts[3])))
+                    self.max_mhz = float(parts[2])
+                except (ValueError, IndexError):
+                    pass
         if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
-        busy = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "source": self.mode}
+        busy = [x for x in self.samples if not (x[1] & 0x1)] or self.samples
         mask = 0
-        for s in busy:
-            mask |= s[1]
+        for x in busy:
+            mask |= x[1]
         return {
-            "sm_mhz": statistics.median(s[0] for s in busy),
+            "sm_mhz": statistics.median(x[0] for x in busy),
             "sm_max_mhz": self.max_mhz,
             "reasons": [n for bit, n in _REASONS.items() if mask & bit and bit != 0x1],
-            "power_w_max": round(max(s[2] for s in busy), 1),
+            "power_w_max": round(max(x[2] for x in busy), 1),
             "samples": len(busy),
-            "source": "nvml",
+            "gpus": len(self.indices),
+            "source": "nvidia-smi" if self.mode == "smi" else self.mode,
         }
+
+
+def _node_gpu_indices(world):
+    """nvidia-smi / NVML indices of the GPUs this job uses (CUDA_VISIBLE_DEVICES
+    order, one per rank)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if all(x.isdigit() for x in ids):
+            return [int(x) for x in ids[:world]]
+    return list(range(world))
 
 
 def dist_env():
@@ -256,7 +297,6 @@ def workload_config(world):
         "global_batch": BATCH, "T": 1, "num_qk_heads": H, "num_v_heads": HV, "head_dim": DIM,
         "state": "fp32 [256,32,128,128] k-last, updated in place",
         "parallelism": f"tp{world}",
-        "l2": "inputs larger than L2 (512 MiB state per step at N=1; no flush)",
     }
 
 
@@ -294,28 +334,36 @@ def b1_latency(device, iters=200):
     return res
 
 
-def parity_check(step_inputs, device, step_fn, shard):
-    """Runs one step and compares 4 sampled batch entries (all local heads)
-    with the oracle; returns a summary dict."""
-    from gdn_b200 import synthetic
-    from oracle import gdn_ref
-
-    q, k, v, state, A_log, a, dt_bias, b, scale = step_inputs
-    sel = torch.tensor([0, 1, BATCH // 2, BATCH - 1], device=device)
-    sub = synthetic.GdnInputs(q[sel].cpu(), k[sel].cpu(), v[sel].cpu(), state[sel].cpu(),
-                              A_log.cpu(), a[sel].cpu(), dt_bias.cpu(), b[sel].cpu(), scale)
+def sanity_check(state, device, step_fn):
+    """Runs the first step and checks, without any reference, that every output
+    element is finite and that the state changed (parity with the reference is
+    the GPU tests' job)."""
+    before = state[:2].clone()
     out = step_fn()
     torch.cuda.synchronize(device)
-    want_out, want_state = gdn_ref.decode(*sub.args())
-    hv0, hv1 = shard.hv0, shard.hv1
-    got_out = out[sel][:, :, hv0:hv1].float().cpu()
-    got_state = state[sel].cpu()
-    e_out = (got_out - want_out.float()).abs()
-    e_st = (got_state - want_state).abs()
-    ok_out = bool(torch.all(e_out <= 1e-2 + 1e-2 * want_out.float().abs()))
-    ok_st = bool(torch.all(e_st <= 1e-3 + 1e-3 * want_state.abs()))
-    return {"sampled_entries": 4, "max_abs_err_output": float(e_out.max()),
-            "max_abs_err_state": float(e_st.max()), "ok": ok_out and ok_st}
+    return {"outputs_finite": bool(torch.isfinite(out.float()).all()),
+            "state_updated": bool(not torch.equal(before, state[:2]))}
+
+
+class _PlainGraph:
+    """Single-GPU steps (kernel_cuda_b200 on each argument tuple) recorded as one
+    CUDA graph."""
+
+    def __init__(self, device, step_args, out):
+        import gdn_b200
+
+        self.graph = torch.cuda.CUDAGraph()
+        self.out = out
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.graph(self.graph, stream=stream):
+            for a in step_args:
+                gdn_b200.kernel_cuda_b200(*a, out, a[3])
+        torch.cuda.current_stream(device).wait_stream(stream)
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
 
 
 def run_b200_arm(args, rank, world, local_rank):
@@ -333,54 +381,78 @@ def run_b200_arm(args, rank, world, local_rank):
     shard = HeadShard(rank, world, H, HV)
     hl, hvl = shard.h_local, shard.hv_local
 
-    # local shard inputs, drawn on the device
+    # Local shard inputs, drawn on the device.  Each step updates one "layer's"
+    # state and the next step the next layer's (round robin), like the GDN layers of
+    # a model: with enough layers the per-GPU working set stays >= 3x the L2, so no
+    # step finds its state cached by the previous one (at N=8 one layer's shard is
+    # only 64 MiB).  q/k/v/a/b are shared by the layers.
     inp = synthetic.make_inputs(B=BATCH, H=hl, HV=hvl, seed=1234 + rank, device=device)
+    l2_bytes = torch.cuda.get_device_properties(device).L2_cache_size
+    state_bytes = inp.state.numel() * inp.state.element_size()
+    layers = max(1, math.ceil(3 * l2_bytes / state_bytes))
+    gen = torch.Generator(device=device).manual_seed(99 + rank)
+    states = [inp.state] + [torch.randn(inp.state.shape, generator=gen, device=device).mul_(0.1)
+                            for _ in range(layers - 1)]
     out = torch.empty((BATCH, 1, HV, DIM), dtype=torch.bfloat16, device=device)
     tp = (TPDecode(H=H, HV=HV, max_batch=BATCH, device=device, collective=args.tp_collective)
           if world > 1 else None)
 
-    # N > 1: the step (decode + exchange) is captured once as CUDA graphs and
-    # replayed, so host-side Python does not bound the ~20-80 us per-rank step.
-    graphs = tp.capture(*inp.args()) if tp is not None else None
+    def layer_args(i):
+        return (inp.q, inp.k, inp.v, states[i % layers], inp.A_log, inp.a, inp.dt_bias, inp.b,
+                inp.scale)
 
-    def step(events=None):
-        if events is not None:
-            events[0].record()
-        if graphs is not None:
-            res = graphs.replay()
-        else:
-            gdn_b200.kernel_cuda_b200(*inp.args(), out, inp.state)
-            res = out
-        if events is not None:
-            events[1].record()
+    def eager_step(i):
+        """One step of layer i through the public API."""
+        if tp is not None:
+            return tp.step(*layer_args(i), out=None if tp.collective == "peer" else out)
+        gdn_b200.kernel_cuda_b200(*layer_args(i), out, states[i % layers])
+        return out
+
+    # The timed region is one CUDA graph of all K steps (layer i % layers at step i),
+    # as a model's decode graph holds all its layers: no host work and no graph
+    # boundaries inside it (separate replays of short graphs left 40-60 us idle
+    # gaps between them at N > 1).
+    K = args.steps
+    seq = [layer_args(i) for i in range(K)]
+    graph = tp.capture_sequence(seq) if tp is not None else _PlainGraph(device, seq, out)
+
+    step_no = [0]
+
+    def step():
+        res = eager_step(step_no[0])
+        step_no[0] += 1
         return res
 
-    parity = parity_check(inp.args(), device, step, shard)
+    sanity = sanity_check(states[0], device, step)
     for _ in range(args.warmup):
         step()
+    graph.replay()                                        # upload + warm the graph, untimed
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    # Set up the sampler (NVML initialisation takes milliseconds) before the ranks
+    # line up: anything slow between the barrier and a rank's launch shows up in
+    # the other ranks' timings, which wait for it at the first in-graph barrier.
+    sampler = ClockSampler(_node_gpu_indices(world), mode=args.clock_sampler
+                           if rank == 0 else "none")
     torch.cuda.synchronize(device)
     if world > 1:
         torch.distributed.barrier()
-
-    K = args.steps
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(K)]
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local_rank)
-    sampler.start()
+        torch.cuda.synchronize(device)
     wall0 = time.perf_counter()
     t_start.record()
-    for i in range(K):
-        step(ev[i])
+    graph.replay()
     t_end.record()
+    # The timed region is queued before sampling starts, so the sampler runs while
+    # the GPU executes it and cannot delay a launch (measured: a sampler active
+    # during enqueueing cost 17-170 % at N=8, a ~29 us step).
+    sampler.start()
     torch.cuda.synchronize(device)
     wall = time.perf_counter() - wall0
     clocks = sampler.stop()
     if world > 1:
         torch.distributed.barrier()
     elapsed_ms = t_start.elapsed_time(t_end)
-    kernel_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev)
+    kernel_ms = elapsed_ms / K          # steps run back to back inside the graph
     elapsed_ms_max = max_over_ranks(elapsed_ms, world, device)
 
     total_bytes = synthetic.bytes_per_call(BATCH)            # whole job, all heads
@@ -397,7 +469,7 @@ def run_b200_arm(args, rank, world, local_rank):
     def e2e_step():
         for n, t in host.items():
             getattr(inp, n).copy_(t, non_blocking=True)
-        res = step()
+        res = step()                       # public API call, next layer's state
         out_host.copy_(res, non_blocking=True)
 
     for _ in range(3):
@@ -433,7 +505,7 @@ def run_b200_arm(args, rank, world, local_rank):
         if tp.collective == "peer":
             tp.check()
         torch.distributed.barrier()
-        del graphs, tp
+        del graph, tp
         torch.distributed.destroy_process_group()
     if rank != 0:
         return
@@ -448,7 +520,10 @@ def run_b200_arm(args, rank, world, local_rank):
         "warmup": args.warmup, "ms_per_step": round(elapsed_ms_max / K, 5),
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
-        "config": workload_config(world),
+        "config": dict(workload_config(world), l2=(
+            f"inputs larger than L2, no flush: {layers} layer state(s) of {state_bytes >> 20} MiB "
+            f"per GPU updated round robin ({(layers * state_bytes) >> 20} MiB >= 3x the "
+            f"{l2_bytes >> 20} MiB L2)"), timed_loop=f"one CUDA graph of the {K} steps"),
         "latency_b1_us": latency,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
@@ -466,7 +541,7 @@ def run_b200_arm(args, rank, world, local_rank):
         "gpu_launches": launches_per_step * K,
         "clocks": clocks,
         "cpu_baseline": cpu,
-        "parity": parity,
+        "sanity": sanity,
         "wall_s_timed": round(wall, 4),
     }
     print(json.dumps(line), flush=True)
@@ -536,6 +611,8 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--skip-b1", action="store_true", help="omit the B=1 latency leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--clock-sampler", choices=["nvml", "smi", "none"], default="nvml",
+                    help="how rank 0 samples clocks during the timed region")
     ap.add_argument("--tp-collective", choices=["peer", "nccl"], default="peer",
                     help="output exchange at N > 1: fused peer stores (default) or NCCL")
     args = ap.parse_args()

@@ -177,30 +177,44 @@ class TPDecode:
         return self._buf[start:start + nbytes].view(torch.bfloat16).view(B, 1, self.shard.HV, self.V)
 
     @torch.no_grad()
-    def capture(self, q, k, v, state, A_log, a, dt_bias, b, scale) -> "CapturedSteps":
-        """Record this rank's step on these (fixed) input tensors as CUDA graphs.
+    def capture(self, q, k, v, state, A_log, a, dt_bias, b, scale,
+                steps: int = 1) -> "CapturedSteps":
+        """Record ``steps`` consecutive steps on these (fixed) input tensors as CUDA
+        graphs; see ``capture_sequence``."""
+        return self.capture_sequence([(q, k, v, state, A_log, a, dt_bias, b, scale)] * steps)
 
-        Replaying a graph runs the step on whatever the tensors hold at that time,
-        with no host work besides the graph launch.  The peer exchange alternates
-        two output buffers, so two graphs are recorded (one per buffer) and
-        ``CapturedSteps.replay`` alternates them; every rank must replay the same
-        number of steps.  Nothing is executed while capturing."""
-        B = q.shape[0]
+    @torch.no_grad()
+    def capture_sequence(self, step_args) -> "CapturedSteps":
+        """Record one step per entry of ``step_args`` (tuples of the ``step``
+        arguments, e.g. one per model layer with that layer's state) as CUDA graphs.
+
+        Replaying runs the steps on whatever the tensors hold at that time, with no
+        host work besides one graph launch (several steps per graph amortise it, as a
+        model's decode graph does over its layers).  The peer exchange alternates two
+        output buffers, so one graph is recorded per starting buffer and each replay
+        picks the one that continues this object's step count (captures and eager
+        steps can be mixed).  Every rank must replay the same number of steps.
+        Nothing runs while capturing."""
+        step_args = list(step_args)
+        if not step_args:
+            raise ValueError("nothing to capture")
         graphs, outs = [], []
         stream = torch.cuda.Stream(self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
-        for parity in (0, 1):
+        for start in (0, 1):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                if self.collective == "peer":
-                    out = self._peer_step(q, k, v, state, A_log, a, dt_bias, b, scale, B, None,
-                                          parity=parity)
-                else:
-                    out = self.step(q, k, v, state, A_log, a, dt_bias, b, scale)
+                for i, args in enumerate(step_args):
+                    parity = (start + i) & 1
+                    if self.collective == "peer":
+                        out = self._peer_step(*args, args[0].shape[0], None, parity=parity)
+                    else:
+                        out = self.step(*args)
             graphs.append(g)
             outs.append(out)
         torch.cuda.current_stream(self.device).wait_stream(stream)
-        return CapturedSteps(self, graphs, outs)
+        return CapturedSteps(self, graphs, outs, len(step_args))
+
     def check(self) -> None:
         """Raise if a cross-rank wait of the peer exchange has timed out (syncs)."""
         if self.collective == "peer" and int(self.status.item()) != 0:
@@ -247,18 +261,17 @@ class TPDecode:
 
 
 class CapturedSteps:
-    """Two recorded TP steps (see ``TPDecode.capture``), replayed alternately."""
+    """Recorded TP steps (see ``TPDecode.capture``)."""
 
-    def __init__(self, tp: TPDecode, graphs, outs):
-        self.tp, self.graphs, self.outs = tp, graphs, outs
+    def __init__(self, tp: TPDecode, graphs, outs, steps: int):
+        self.tp, self.graphs, self.outs, self.steps = tp, graphs, outs, steps
         self.count = 0
 
     def replay(self) -> torch.Tensor:
-        """Run one step; returns its output [B, 1, HV, V] (valid until the
-        next-but-one replay)."""
-        i = self.count & 1
+        """Run the recorded steps once; returns the last step's output
+        [B, 1, HV, V] (valid until that buffer is written again two steps later)."""
+        i = self.tp._steps & 1
         self.graphs[i].replay()
         self.count += 1
-        if self.tp.collective == "peer":
-            self.tp._steps += 1
+        self.tp._steps += self.steps
         return self.outs[i]

@@ -155,7 +155,16 @@ def test_fused_step_replays_from_cuda_graphs():
             torch.cuda.synchronize()
             assert torch.equal(out, want) and torch.equal(g.state, h.state), i
         assert int(tp._epoch.item()) == 5 and int(tp.status.item()) == 0
-        del steps
+        # four steps per graph, replayed twice, after the odd count above
+        many = tp.capture(*g.args(), steps=4)
+        for i in range(2):
+            out = many.replay()
+            for _ in range(4):
+                want, _ = gdn_b200.gdn_decode(*h.args())
+            torch.cuda.synchronize()
+            assert torch.equal(out, want) and torch.equal(g.state, h.state), i
+        assert int(tp._epoch.item()) == 13 and tp._steps == 13
+        del steps, many
     finally:
         dist.destroy_process_group()
 
