@@ -583,6 +583,24 @@ def run_sweep(device):
     res["pooled"] = {"pool": P, "B": B, "active": B - 1, "median_us": round(med, 3),
                      "GBps": round(nb / med / 1e3, 1)}
     del inp, out
+    # bf16-stored state (FlashInfer's bf16-state backend): half the state bytes
+    res["bf16_state"] = []
+    for B, flushed in ((1, True), (256, False)):
+        inp = synthetic.make_inputs(B=B, seed=B, device=device)
+        inp.state = inp.state.to(torch.bfloat16)
+        out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
+        flush_buf = l2_flush_buffer(device) if flushed else None
+        fn = lambda: gdn_b200.decode_bf16_state(  # noqa: E731
+            inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale, out)
+        for _ in range(10):
+            fn()
+        med = statistics.median(cupti_kernel_durations_us(
+            fn, 100 if flushed else 50, device, flush=None if flush_buf is None else flush_buf.zero_))
+        nb = synthetic.bytes_per_call(B, state_elem_bytes=2)
+        res["bf16_state"].append({"B": B, "median_us": round(med, 3),
+                                  "GBps": round(nb / med / 1e3, 1),
+                                  "l2": "flushed" if flushed else "inputs > L2"})
+        del inp, out
     for T in (2, 4):
         B = 64
         inp = synthetic.make_inputs(B=B, T=T, seed=T, device=device)

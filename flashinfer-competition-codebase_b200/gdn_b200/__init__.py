@@ -8,6 +8,7 @@ from ._lib import GdnError, load as load_library  # noqa: F401
 from .ops import (  # noqa: F401
     ALGO_ENTRY_POINTS,
     ALGO_NO_DPS,
+    decode_bf16_state,
     decode_tuned,
     gated_delta_rule_decode_pretranspose,
     gated_delta_rule_mtp,
@@ -24,6 +25,7 @@ __all__ = [
     "gdn_decode",
     "gated_delta_rule_decode_pretranspose",
     "gated_delta_rule_mtp",
+    "decode_bf16_state",
     "decode_tuned",
     "interleave_heads",
     "ALGO_ENTRY_POINTS",

@@ -32,6 +32,11 @@ SIGNATURES = {
         [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _D, _P, _P, _I, _I,
          _I, _I, _I, _I, _I, _I, _I, _P, _P],
     ),
+    "gdn_decode_bf16_state": (
+        _I,
+        [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _D, _P, _P, _I, _I,
+         _I, _I, _I, _I, _I, _I, _I, _P, _P],
+    ),
     "gdn_decode_tuned": (
         _I,
         [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _D, _P,

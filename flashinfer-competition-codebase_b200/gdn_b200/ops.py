@@ -150,7 +150,7 @@ def gated_delta_rule_decode_pretranspose(
     use_qk_l2norm: bool = True, initial_state=None, initial_state_indices=None,
     output_state_indices=None, bad_index_count=None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
-    """FlashInfer-compatible fp32 k-last decode (flashinfer/gdn_decode.py:118-195).
+    """FlashInfer-compatible k-last decode (flashinfer/gdn_decode.py:118-261).
 
     Without a pool, ``state`` [B,HV,V,K] is updated in place.  With
     ``initial_state`` [pool,HV,V,K] and ``initial_state_indices`` [B], entry i
@@ -159,7 +159,9 @@ def gated_delta_rule_decode_pretranspose(
     A negative read index skips the entry and writes a zero output row; a
     negative write index redirects the write to slot 0.  Out-of-range indices
     are skipped and, if ``bad_index_count`` (an int32 CUDA tensor of one
-    element) is given, counted into it.  Returns ``(output, state_or_pool)``.
+    element) is given, counted into it.  An fp32 state takes T == 1; a bf16 state
+    (``decode_bf16_state``) takes T >= 1, like FlashInfer's bf16-state backend.
+    Returns ``(output, state_or_pool)``.
     """
     use_pool = initial_state is not None
     if use_pool != (initial_state_indices is not None):
@@ -168,6 +170,16 @@ def gated_delta_rule_decode_pretranspose(
         raise ValueError("output_state_indices can only be used with initial_state (pool mode)")
     if not use_pool and state is None:
         raise ValueError("either state or initial_state must be provided")
+    st = initial_state if use_pool else state
+    if isinstance(st, torch.Tensor) and st.dtype == _BF16:
+        # bf16 state: FlashInfer's bf16-state backend (flashinfer/gdn_decode.py:255-261),
+        # T = 1 or several tokens
+        output = decode_bf16_state(
+            q, k, v, st, A_log, a, dt_bias, b, scale=scale, output=output,
+            state_indices=initial_state_indices if use_pool else None,
+            output_state_indices=output_state_indices, use_qk_l2norm=use_qk_l2norm,
+            bad_index_count=bad_index_count)
+        return output, st
     B, T, H, HV, K, V, dev = _check_step_inputs(q, k, v, A_log, a, dt_bias, b)
     if T != 1:
         raise ValueError("the fp32-state decode takes T == 1; use gated_delta_rule_mtp for T > 1")
@@ -196,6 +208,55 @@ def gated_delta_rule_decode_pretranspose(
             int(bool(use_qk_l2norm)), _ptr(bad_index_count), _stream_handle(dev),
         )
     return output, initial_state
+
+
+@torch.no_grad()
+def decode_bf16_state(q, k, v, state_pool, A_log, a, dt_bias, b, scale=None, output=None,
+                      state_indices=None, output_state_indices=None,
+                      intermediate_states_buffer=None, disable_state_update: bool = False,
+                      use_qk_l2norm: bool = False, bad_index_count=None) -> torch.Tensor:
+    """Decode with the state stored in bf16, T >= 1 tokens, updated in place.
+
+    ``state_pool`` [pool, HV, V, K] bf16; entry i uses slot ``state_indices[i]``
+    (``None``: slot i) and writes ``output_state_indices[i]`` (default: the read
+    slot), with the index rules of the pooled fp32 path.  The math is fp32; the
+    state is rounded to bf16 when stored.  ``intermediate_states_buffer``
+    [>= B, cache_steps >= T, HV, V, K] bf16 receives the state after each token.
+    Returns the output [B, T, HV, V] bf16.  C entry: ``gdn_decode_bf16_state``.
+    """
+    B, T, H, HV, K, V, dev = _check_step_inputs(q, k, v, A_log, a, dt_bias, b)
+    pool = state_pool.shape[0] if state_pool.dim() == 4 else -1
+    _check(state_pool, "state_pool", _BF16, (pool, HV, V, K), dev)
+    idx = None if state_indices is None else _index_tensor(state_indices, "state_indices", B, dev)
+    oidx = None
+    if output_state_indices is not None:
+        if idx is None:
+            raise ValueError("output_state_indices needs state_indices")
+        oidx = _index_tensor(output_state_indices, "output_state_indices", B, dev)
+    if idx is None and pool < B:
+        raise ValueError(f"state_pool holds {pool} slots; without indices it needs >= B={B}")
+    if output is None:
+        output = torch.empty((B, T, HV, V), dtype=_BF16, device=dev)
+    _check(output, "output", _BF16, (B, T, HV, V), dev)
+    cache_steps = 0
+    if intermediate_states_buffer is not None:
+        ib = intermediate_states_buffer
+        if ib.dim() != 5 or ib.shape[0] < B or ib.shape[1] < T or tuple(ib.shape[2:]) != (HV, V, K):
+            raise ValueError(
+                f"intermediate_states_buffer must be [>= {B}, >= {T}, {HV}, {V}, {K}], got {tuple(ib.shape)}")
+        _check(ib, "intermediate_states_buffer", _BF16, None, dev)
+        cache_steps = ib.shape[1]
+    if bad_index_count is not None:
+        _check(bad_index_count, "bad_index_count", torch.int32, (1,), dev)
+    with torch.cuda.device(dev):
+        _lib.call(
+            "gdn_decode_bf16_state", q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            state_pool.data_ptr(), pool, _ptr(idx), _ptr(oidx), A_log.data_ptr(), a.data_ptr(),
+            dt_bias.data_ptr(), b.data_ptr(), _resolve_scale(scale, K), output.data_ptr(),
+            _ptr(intermediate_states_buffer), cache_steps, int(bool(disable_state_update)),
+            B, T, H, HV, K, V, int(bool(use_qk_l2norm)), _ptr(bad_index_count),
+            _stream_handle(dev))
+    return output
 
 
 _warned_mtp_default = False

@@ -85,13 +85,14 @@ def make_pool_indices(B: int, pool: int, seed: int = 0, n_pad: int = 1,
 
 def bytes_per_call(B: int, T: int = 1, H: int = 16, HV: int = 32, K: int = 128, V: int = 128,
                    active: Optional[int] = None, intermediates: bool = False,
-                   write_final: bool = True) -> int:
+                   write_final: bool = True, state_elem_bytes: int = 4) -> int:
     """Algorithmic HBM bytes of one call: state read once and written once per
     active entry (plus one write per token when intermediates are kept), and
-    every input and output element once.  For T=1 and the Qwen3-Next shapes this
-    is 4,219,008 * B + 256 bytes."""
+    every input and output element once.  For T=1, an fp32 state and the
+    Qwen3-Next shapes this is 4,219,008 * B + 256 bytes (state_elem_bytes=2 for a
+    bf16 state)."""
     n = B if active is None else active
-    state = HV * V * K * 4
+    state = HV * V * K * state_elem_bytes
     traffic = n * state * (1 + (1 if write_final else 0) + (T if intermediates else 0))
     qk = 2 * B * T * H * K * 2
     vv = B * T * HV * V * 2

@@ -143,6 +143,42 @@ GDN_API int gdn_decode_mtp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16*
                    void* stream);
 
 /*
+ * Decode with the state stored in bf16 (T >= 1, optional pool), updated in place.
+ *
+ * Replaces the bf16-state backend of FlashInfer's k-last decode, which
+ * gated_delta_rule_decode_pretranspose selects for a bf16 state with K = V = 128
+ * (flashinfer/gdn_decode.py:255-261; kernels in
+ * flashinfer/gdn_kernels/gdn_decode_bf16_state.py, T = 1 and multi-token, with
+ * split read/write pool slots at :124-172).  The reference's own decode keeps
+ * an fp32 state; this variant halves the state bytes, which dominate the traffic.
+ * Arithmetic is fp32 as in the other entries: the state is widened on load,
+ * and rounded to bf16 (nearest even) only when stored.
+ *  - state_pool [pool_size, HV, V, K] bf16; entry i uses slot
+ *    state_indices[i] (NULL: slot i, pool_size >= B), writes slot
+ *    output_state_indices[i] if given (NULL: the read slot; requires
+ *    state_indices).  Index rules as gdn_decode_pooled: a negative read index
+ *    skips the entry with zero outputs (FlashInfer's bf16 backend instead
+ *    redirects it to a reserved slot 0 and leaves the output undefined; callers
+ *    that reserve slot 0 see no difference), out-of-range indices are skipped
+ *    and counted in *bad_index_count.
+ *  - T tokens run in order per entry; intermediate_states [B, cache_steps, HV,
+ *    V, K] bf16 (may be NULL) receives the state after each token; the final
+ *    state is written back unless disable_state_update != 0.
+ *  - q and k must be 16-byte aligned (16-byte chunks of 8 values are loaded).
+ */
+GDN_API int gdn_decode_bf16_state(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                                  gdn_bf16* state_pool, int pool_size,
+                                  const int32_t* state_indices,
+                                  const int32_t* output_state_indices,
+                                  const float* A_log, const gdn_bf16* a,
+                                  const float* dt_bias, const gdn_bf16* b, double scale,
+                                  gdn_bf16* output, gdn_bf16* intermediate_states,
+                                  int cache_steps, int disable_state_update,
+                                  int B, int T, int H, int HV, int K, int V,
+                                  int use_qk_l2norm, int32_t* bad_index_count,
+                                  void* stream);
+
+/*
  * Launch-shape tuning entry (no counterpart in the reference, whose launch
  * shapes are fixed: solution/cuda/kernel.cu:234-235, :423-424).  Same step
  * as gdn_decode_mtp without intermediates (T == 1: gdn_decode_pooled with

@@ -187,3 +187,32 @@ def decode_mtp(q, k, v, pool, state_indices, A_log, a, dt_bias, b, scale,
     if not disable_state_update:
         new_pool[slots] = S
     return output, new_pool, inter
+
+
+@torch.no_grad()
+def decode_bf16_state(q, k, v, pool, state_indices, A_log, a, dt_bias, b, scale,
+                      output_state_indices: Optional[torch.Tensor] = None,
+                      keep_intermediates: bool = False, disable_state_update: bool = False,
+                      use_qk_l2norm: bool = False):
+    """A state stored in bf16 (FlashInfer's bf16-state backend, flashinfer/gdn_decode.py:255-261):
+    the state is widened to fp32, the T tokens run with the fp32 steps of decode_mtp, and
+    every state that is stored (intermediates, final) is rounded to bf16 (nearest even).
+    Slots follow decode_pooled: a read index < 0 or >= pool size skips the entry with
+    zero outputs; the final state goes to output_state_indices[i] (default: the read
+    slot), a negative write index meaning slot 0, an out-of-range one dropping it.
+    Returns (output [B,T,HV,V] bf16, new_pool bf16, intermediates bf16 or None)."""
+    B, T = q.shape[0], q.shape[1]
+    P = pool.shape[0]
+    idx = list(range(B)) if state_indices is None else state_indices.long().tolist()
+    oidx = idx if output_state_indices is None else output_state_indices.long().tolist()
+    out, _, inter = decode_mtp(q, k, v, pool.float(), state_indices, A_log, a, dt_bias, b, scale,
+                               keep_intermediates=True, disable_state_update=True,
+                               use_qk_l2norm=use_qk_l2norm)
+    new_pool = pool.clone()
+    if not disable_state_update:
+        for i in range(B):
+            if 0 <= idx[i] < P:
+                w = oidx[i] if oidx[i] >= 0 else 0
+                if w < P:
+                    new_pool[w] = inter[i, T - 1].to(torch.bfloat16)
+    return out, new_pool, (inter.to(torch.bfloat16) if keep_intermediates else None)
