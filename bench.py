@@ -585,7 +585,7 @@ def run_sweep(device):
     del inp, out
     # bf16-stored state (FlashInfer's bf16-state backend): half the state bytes
     res["bf16_state"] = []
-    for B, flushed in ((1, True), (256, False)):
+    for B, flushed in ((1, True), (64, False), (256, False)):
         inp = synthetic.make_inputs(B=B, seed=B, device=device)
         inp.state = inp.state.to(torch.bfloat16)
         out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
