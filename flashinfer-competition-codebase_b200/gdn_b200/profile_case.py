@@ -1,6 +1,6 @@
 """A small, fixed decode case for profiler captures (ncu) of the decode kernel.
 
-    python -m gdn_b200.profile_case --batch 128 --launches 3 [--T 1] [--pooled]
+    python -m gdn_b200.profile_case --batch 128 --launches 3 [--T 1] [--pooled] [--bf16-state]
 
 Runs ``--launches`` decode steps of the Qwen3-Next shapes (16 q/k heads, 32
 v-heads, K = V = 128) at the given batch on cuda:0 and exits.  Batch 128
@@ -27,6 +27,7 @@ def main():
     ap.add_argument("--lanes-per-row", type=int, default=0)
     ap.add_argument("--rows-per-lane", type=int, default=0)
     ap.add_argument("--warps-per-cta", type=int, default=0)
+    ap.add_argument("--bf16-state", action="store_true", help="bf16-stored state variant")
     args = ap.parse_args()
     dev = torch.device("cuda:0")
     B, T = args.batch, args.T
@@ -34,6 +35,15 @@ def main():
     inp = synthetic.make_inputs(B=B, T=T, slots=slots, seed=0, device=dev)
     idx = synthetic.make_pool_indices(B, slots, seed=0, n_pad=1, device=dev) if args.pooled else None
     out = torch.empty((B, T, 32, 128), dtype=torch.bfloat16, device=dev)
+    if args.bf16_state:
+        inp.state = inp.state.to(torch.bfloat16)
+        for _ in range(args.launches):
+            gdn_b200.decode_bf16_state(inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a,
+                                       inp.dt_bias, inp.b, inp.scale, out, state_indices=idx)
+        torch.cuda.synchronize(dev)
+        print(f"profile_case ok: B={B} T={T} pooled={args.pooled} bf16 state "
+              f"launches={args.launches}")
+        return
     for _ in range(args.launches):
         gdn_b200.decode_tuned(inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias,
                               inp.b, inp.scale, out, state_indices=idx,
