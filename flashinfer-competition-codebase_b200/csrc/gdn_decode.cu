@@ -127,9 +127,11 @@ __device__ __forceinline__ void st_state_u4(void* ptr, const uint4& x) {
                "r"(x.z), "r"(x.w)
                : "memory");
 }
-// two fp32 -> packed bf16x2, round to nearest even (low half = first value)
+// two fp32 -> packed bf16x2 in one paired conversion, each rounded to nearest even
+// (low half = first value)
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return static_cast<uint32_t>(f32_to_bf16(lo)) | (static_cast<uint32_t>(f32_to_bf16(hi)) << 16);
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 // One 16-byte chunk of a state row in the state's storage type, widened to fp32
