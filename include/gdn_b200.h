@@ -3,10 +3,12 @@
  *
  * One library, libgdn_b200.so, holds every kernel of the GDN decode path:
  * the fused T=1 decode step, the pooled-state (continuous batching) step,
- * the multi-token (speculative verify) step and the head interleave used
- * after a tensor-parallel all-gather.  No function here allocates memory:
- * the caller owns every buffer.  No function synchronises the host: work
- * is enqueued on the given stream (NULL = the legacy default stream).
+ * the multi-token (speculative verify) step, the bf16-state variant, the
+ * tensor-parallel step that stores its outputs into every rank's buffer
+ * over NVLink, and the head interleave used after an NCCL all-gather.  No
+ * function here allocates memory: the caller owns every buffer.  No
+ * function synchronises the host: work is enqueued on the given stream
+ * (NULL = the legacy default stream).
  *
  * Data layout (all tensors contiguous, row-major):
  *   q, k        [B, T, H,  K]   bf16
@@ -15,6 +17,7 @@
  *   A_log       [HV]            fp32
  *   dt_bias     [HV]            fp32
  *   state       [S, HV, V, K]   fp32   "k-last": K is the contiguous axis
+ *                                      (bf16 in gdn_decode_bf16_state)
  *   output      [B, T, HV, V]   bf16
  * with K == V == 128, HV % H == 0 (v-head hv reads q/k head hv / (HV/H)).
  *
