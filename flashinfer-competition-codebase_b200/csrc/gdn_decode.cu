@@ -34,7 +34,7 @@
 
 #include <mutex>
 
-#include "../../include/gdn_b200.h"
+#include "gdn_b200.h"
 
 namespace {
 

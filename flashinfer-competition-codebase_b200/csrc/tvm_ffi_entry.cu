@@ -17,7 +17,7 @@
 #include <tvm/ffi/extra/c_env_api.h>
 #include <tvm/ffi/function.h>
 
-#include "../../include/gdn_b200.h"
+#include "gdn_b200.h"
 
 namespace {
 
