@@ -130,3 +130,34 @@ def test_head_shard_rules():
         HeadShard(0, 3, 16, 32)
     with pytest.raises(ValueError):
         HeadShard(2, 2, 16, 32)
+
+
+def test_captured_steps_follow_the_shared_step_parity():
+    """CapturedSteps.replay picks the graph recorded for the output buffer the TP
+    object's step count has reached, and advances that count by the steps it ran."""
+    _setup_paths()
+    from gdn_b200.tp import CapturedSteps
+
+    class FakeGraph:
+        def __init__(self, log, name):
+            self.log, self.name = log, name
+
+        def replay(self):
+            self.log.append(self.name)
+
+    class FakeTP:
+        collective = "peer"
+        _steps = 0
+
+    log = []
+    tp = FakeTP()
+    three = CapturedSteps(tp, [FakeGraph(log, "3@even"), FakeGraph(log, "3@odd")],
+                          ["out-even", "out-odd"], 3)
+    two = CapturedSteps(tp, [FakeGraph(log, "2@even"), FakeGraph(log, "2@odd")],
+                        ["o2-even", "o2-odd"], 2)
+    assert three.replay() == "out-even" and tp._steps == 3
+    assert three.replay() == "out-odd" and tp._steps == 6
+    assert two.replay() == "o2-even" and tp._steps == 8      # mixing captures keeps the count
+    tp._steps += 1                                              # an eager step in between
+    assert two.replay() == "o2-odd" and tp._steps == 11
+    assert log == ["3@even", "3@odd", "2@even", "2@odd"]
