@@ -111,73 +111,95 @@ def save(name, meta, **arrays):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("GDN_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--only", default=None, help="comma-separated fixture names to (re)make")
     args = ap.parse_args()
     ref, prefill_ref = load_reference(args.reference)
     torch.manual_seed(0)
+    only = None if args.only is None else set(args.only.split(","))
+
+    def want(name):
+        return only is None or name in only
 
     # 1. The contest definition's shape (4 q/k heads, 8 v-heads), B=1.
-    meta = dict(B=1, T=1, H=4, HV=8, seed=0)
-    inp = make_inputs(B=1, H=4, HV=8, seed=0)
-    o, s = ref(*inp.args())
-    save("decode_qk4v8_b1", dict(meta, sha256=input_digest(inp)), output=bf16_bits(o),
-         new_state=s.numpy())
+    if want("decode_qk4v8_b1"):
+        meta = dict(B=1, T=1, H=4, HV=8, seed=0)
+        inp = make_inputs(B=1, H=4, HV=8, seed=0)
+        o, s = ref(*inp.args())
+        save("decode_qk4v8_b1", dict(meta, sha256=input_digest(inp)), output=bf16_bits(o),
+             new_state=s.numpy())
 
     # 2. Gate edge cases and scale=0, B=2.
-    meta = dict(B=2, T=1, H=4, HV=8, seed=1, edits=EDGE_EDITS)
-    inp = apply_edits(make_inputs(B=2, H=4, HV=8, seed=1), EDGE_EDITS)
-    o, s = ref(*inp.args())
-    save("decode_qk4v8_b2_edge", dict(meta, sha256=input_digest(inp)), output=bf16_bits(o),
-         new_state=s.numpy())
+    if want("decode_qk4v8_b2_edge"):
+        meta = dict(B=2, T=1, H=4, HV=8, seed=1, edits=EDGE_EDITS)
+        inp = apply_edits(make_inputs(B=2, H=4, HV=8, seed=1), EDGE_EDITS)
+        o, s = ref(*inp.args())
+        save("decode_qk4v8_b2_edge", dict(meta, sha256=input_digest(inp)), output=bf16_bits(o),
+             new_state=s.numpy())
 
     # 3. Qwen3-Next heads (16 q/k, 32 v), B=1, via head groups.
-    meta = dict(B=1, T=1, H=16, HV=32, seed=0)
-    inp = make_inputs(B=1, H=16, HV=32, seed=0)
-    o, s = ref_grouped(ref, *inp.args())
-    save("decode_h16hv32_b1", dict(meta, sha256=input_digest(inp)), output=bf16_bits(o),
-         new_state=s.numpy())
+    if want("decode_h16hv32_b1"):
+        meta = dict(B=1, T=1, H=16, HV=32, seed=0)
+        inp = make_inputs(B=1, H=16, HV=32, seed=0)
+        o, s = ref_grouped(ref, *inp.args())
+        save("decode_h16hv32_b1", dict(meta, sha256=input_digest(inp)), output=bf16_bits(o),
+             new_state=s.numpy())
 
     # 4. Multi-token, T=3: the decode reference applied token by token (which gives
     #    the intermediate states), checked against the prefill reference's
     #    sequential loop on the same tokens.
-    B, T = 1, 3
-    meta = dict(B=B, T=T, H=4, HV=8, seed=2)
-    inp = make_inputs(B=B, T=T, H=4, HV=8, seed=2)
-    S = inp.state.clone()
-    outs, inters = [], []
-    for t in range(T):
-        sl = slice(t, t + 1)
-        o, S = ref(inp.q[:, sl], inp.k[:, sl], inp.v[:, sl], S, inp.A_log, inp.a[:, sl],
-                   inp.dt_bias, inp.b[:, sl], inp.scale)
-        outs.append(o)
-        inters.append(S.clone())
-    out_loop = torch.cat(outs, dim=1)                      # [B,T,HV,V]
-    inter = torch.stack(inters, dim=1)                     # [B,T,HV,V,K]
-    cu = torch.arange(0, (B + 1) * T, T, dtype=torch.int32)
-    flat = lambda x: x.reshape(B * T, *x.shape[2:])        # noqa: E731
-    o_p, s_p = prefill_ref(flat(inp.q), flat(inp.k), flat(inp.v), inp.state, inp.A_log,
-                           flat(inp.a), inp.dt_bias, flat(inp.b), cu, inp.scale)
-    torch.testing.assert_close(o_p.reshape(B, T, *o_p.shape[1:]).float(), out_loop.float(),
-                               rtol=1e-2, atol=1e-2)
-    torch.testing.assert_close(s_p, inter[:, -1], rtol=1e-4, atol=1e-4)
-    save("mtp_qk4v8_b1_t3", dict(meta, sha256=input_digest(inp)), output=bf16_bits(out_loop),
-         intermediates=inter.numpy(), prefill_output=bf16_bits(o_p),
-         prefill_state=s_p.numpy())
+    if want("mtp_qk4v8_b1_t3"):
+        B, T = 1, 3
+        meta = dict(B=B, T=T, H=4, HV=8, seed=2)
+        inp = make_inputs(B=B, T=T, H=4, HV=8, seed=2)
+        S = inp.state.clone()
+        outs, inters = [], []
+        for t in range(T):
+            sl = slice(t, t + 1)
+            o, S = ref(inp.q[:, sl], inp.k[:, sl], inp.v[:, sl], S, inp.A_log, inp.a[:, sl],
+                       inp.dt_bias, inp.b[:, sl], inp.scale)
+            outs.append(o)
+            inters.append(S.clone())
+        out_loop = torch.cat(outs, dim=1)                      # [B,T,HV,V]
+        inter = torch.stack(inters, dim=1)                     # [B,T,HV,V,K]
+        cu = torch.arange(0, (B + 1) * T, T, dtype=torch.int32)
+        flat = lambda x: x.reshape(B * T, *x.shape[2:])        # noqa: E731
+        o_p, s_p = prefill_ref(flat(inp.q), flat(inp.k), flat(inp.v), inp.state, inp.A_log,
+                               flat(inp.a), inp.dt_bias, flat(inp.b), cu, inp.scale)
+        torch.testing.assert_close(o_p.reshape(B, T, *o_p.shape[1:]).float(), out_loop.float(),
+                                   rtol=1e-2, atol=1e-2)
+        torch.testing.assert_close(s_p, inter[:, -1], rtol=1e-4, atol=1e-4)
+        save("mtp_qk4v8_b1_t3", dict(meta, sha256=input_digest(inp)), output=bf16_bits(out_loop),
+             intermediates=inter.numpy(), prefill_output=bf16_bits(o_p),
+             prefill_state=s_p.numpy())
 
     # 5. Pooled state: 5 slots, 3 entries, one padded with -1.  The reference is
     #    run on the gathered active slots; untouched slots keep their values.
-    meta = dict(B=3, T=1, H=4, HV=8, seed=3, slots=5)
-    inp = make_inputs(B=3, H=4, HV=8, seed=3, slots=5)
-    idx = make_pool_indices(3, 5, seed=3, n_pad=1)
-    act = [i for i in range(3) if int(idx[i]) >= 0]
-    sel = torch.tensor(act)
-    slots = idx[sel].long()
-    o, s = ref(inp.q[sel], inp.k[sel], inp.v[sel], inp.state[slots], inp.A_log, inp.a[sel],
-               inp.dt_bias, inp.b[sel], inp.scale)
-    out = torch.zeros(3, 1, 8, 128, dtype=torch.bfloat16)
-    out[sel] = o
-    save("pooled_qk4v8_p5_b3", dict(meta, sha256=input_digest(inp)), output=bf16_bits(out),
-         indices=idx.numpy(), slot_states=s.numpy(), slots=slots.numpy())
+    if want("pooled_qk4v8_p5_b3"):
+        meta = dict(B=3, T=1, H=4, HV=8, seed=3, slots=5)
+        inp = make_inputs(B=3, H=4, HV=8, seed=3, slots=5)
+        idx = make_pool_indices(3, 5, seed=3, n_pad=1)
+        act = [i for i in range(3) if int(idx[i]) >= 0]
+        sel = torch.tensor(act)
+        slots = idx[sel].long()
+        o, s = ref(inp.q[sel], inp.k[sel], inp.v[sel], inp.state[slots], inp.A_log, inp.a[sel],
+                   inp.dt_bias, inp.b[sel], inp.scale)
+        out = torch.zeros(3, 1, 8, 128, dtype=torch.bfloat16)
+        out[sel] = o
+        save("pooled_qk4v8_p5_b3", dict(meta, sha256=input_digest(inp)), output=bf16_bits(out),
+             indices=idx.numpy(), slot_states=s.numpy(), slots=slots.numpy())
 
+    # 6. Multi-token through the reference's own varlen prefill loop: two sequences of
+    #    4 tokens (cu_seqlens [0, 4, 8]), final states and every token's output.
+    if want("mtp_prefill_qk4v8_b2_t4"):
+        B, T = 2, 4
+        meta = dict(B=B, T=T, H=4, HV=8, seed=4)
+        inp = make_inputs(B=B, T=T, H=4, HV=8, seed=4)
+        cu = torch.tensor([0, T, 2 * T], dtype=torch.int32)
+        flat = lambda x: x.reshape(B * T, *x.shape[2:])    # noqa: E731
+        o_p, s_p = prefill_ref(flat(inp.q), flat(inp.k), flat(inp.v), inp.state, inp.A_log,
+                               flat(inp.a), inp.dt_bias, flat(inp.b), cu, inp.scale)
+        save("mtp_prefill_qk4v8_b2_t4", dict(meta, sha256=input_digest(inp)),
+             output=bf16_bits(o_p.reshape(B, T, *o_p.shape[1:])), new_state=s_p.numpy())
 
 if __name__ == "__main__":
     main()

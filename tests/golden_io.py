@@ -21,7 +21,7 @@ from make_golden import apply_edits, input_digest  # noqa: E402
 from gdn_b200.synthetic import make_inputs, make_pool_indices  # noqa: E402
 
 NAMES = ["decode_qk4v8_b1", "decode_qk4v8_b2_edge", "decode_h16hv32_b1", "mtp_qk4v8_b1_t3",
-         "pooled_qk4v8_p5_b3"]
+         "pooled_qk4v8_p5_b3", "mtp_prefill_qk4v8_b2_t4"]
 
 
 def bf16_from_bits(a: np.ndarray) -> torch.Tensor:

@@ -53,6 +53,17 @@ def test_mtp_matches_reference():
     torch.testing.assert_close(pool, gold["prefill_state"], rtol=1e-4, atol=1e-4)
 
 
+def test_mtp_matches_prefill_reference_two_sequences():
+    """Two sequences of 4 tokens through the reference's varlen prefill loop
+    (prefill_kernel.py:85-183 with cu_seqlens [0, 4, 8])."""
+    meta, inp, gold = golden_io.load("mtp_prefill_qk4v8_b2_t4")
+    out, pool, _ = gdn_ref.decode_mtp(inp.q, inp.k, inp.v, inp.state, None, inp.A_log,
+                                      inp.a, inp.dt_bias, inp.b, inp.scale,
+                                      keep_intermediates=False)
+    assert_bf16_close(out, gold["output"])
+    torch.testing.assert_close(pool, gold["new_state"], rtol=1e-4, atol=1e-4)
+
+
 def test_mtp_disable_state_update_keeps_pool():
     meta, inp, gold = golden_io.load("mtp_qk4v8_b1_t3")
     out, pool, inter = gdn_ref.decode_mtp(inp.q, inp.k, inp.v, inp.state, None, inp.A_log,

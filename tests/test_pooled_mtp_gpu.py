@@ -149,6 +149,14 @@ def test_golden_mtp():
     close_state(pool, gold["intermediates"][:, -1])
 
 
+def test_golden_prefill_two_sequences():
+    """The reference's varlen prefill loop on two 4-token sequences (golden fixture)."""
+    meta, inp, gold = golden_io.load("mtp_prefill_qk4v8_b2_t4")
+    out, pool, _ = mtp_call(inp, inter=False)
+    close_out(out, gold["output"])
+    close_state(pool, gold["new_state"])
+
+
 @pytest.mark.parametrize("T", [2, 4])
 def test_mtp_vs_oracle(T):
     """The benchmark's multi-token configuration, scaled down to B=8."""
