@@ -7,7 +7,8 @@
 # (solution/cuda/binding.py:19-28: --use_fast_math via tvm_ffi.cpp.build), with the
 # architecture made explicit for sm_100a because this machine has no GPU to query.
 #
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default $GDN_REFERENCE_ROOT or /root/reference)
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: $GDN_REFERENCE_ROOT, else the
+# checkout location that __graft_entry__.build() also uses)
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
 REF="${1:-${GDN_REFERENCE_ROOT:-/root/reference}}"

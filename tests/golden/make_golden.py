@@ -9,7 +9,7 @@ of the input bytes so the tests can regenerate them and prove they are the
 same.
 
 The reference checkout is needed only here (``--reference``, default
-``$GDN_REFERENCE_ROOT`` or ``/root/reference``); the fixtures themselves are
+``$GDN_REFERENCE_ROOT``, else the default checkout location below); the fixtures are
 self-contained.  Importing ``solution.triton.kernel`` pulls
 ``flashinfer.gdn_decode``, which needs a GPU at import time, so a stub module
 with the one imported name is installed first; the stubbed function is the

@@ -48,9 +48,22 @@ def test_library_has_no_cuda_runtime_dependency(gdn_lib):
 
 def test_abi_version_and_errors(gdn_lib):
     assert gdn_lib.gdn_abi_version() == _lib.ABI_VERSION
-    for code in (0, -1, -2, -3, -4, -5):
-        assert _lib.strerror(code)
+    codes = (_lib.GDN_OK, _lib.GDN_ERR_NULL, _lib.GDN_ERR_SHAPE, _lib.GDN_ERR_ALIGN,
+             _lib.GDN_ERR_LAUNCH, _lib.GDN_ERR_ALIAS, _lib.GDN_ERR_ARG, _lib.GDN_ERR_LIMIT)
+    assert codes == (0, -1, -2, -3, -4, -5, -6, -7)
+    texts = [_lib.strerror(code) for code in codes]
+    assert all(texts) and len(set(texts)) == len(texts)
     assert "unknown" in _lib.strerror(-99)
+
+
+def test_python_error_codes_match_the_header():
+    text = open(HEADER).read()
+    defined = {m.group(1): int(m.group(2))
+               for m in re.finditer(r"^#define\s+(GDN_(?:OK|ERR_\w+))\s+\(?(-?\d+)\)?", text,
+                                    flags=re.M)}
+    assert len(defined) == 8
+    for name, value in defined.items():
+        assert getattr(_lib, name) == value, name
 
 
 def decode_args(**over):
