@@ -532,7 +532,7 @@ def run_b200_arm(args, rank, world, local_rank):
                      "algorithmic_bytes_per_launch": local_bytes},
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": K_e2e, "api": "gdn_b200.kernel_cuda_b200"
-                if world == 1 else "gdn_b200.tp.TPDecode.capture(...).replay()"},
+                if world == 1 else "gdn_b200.tp.TPDecode.step (eager, one call per step)"},
         "tp_exchange": None if world == 1 else (
             "fused: decode kernel stores outputs into every rank's buffer over NVLink, "
             "then a one-CTA barrier kernel (roofline.kernel_us covers both); CUDA graphs"
