@@ -94,3 +94,48 @@ def test_registry_mirrors_reference_shape():
     fns = gdn_b200.load_algo_functions()
     assert set(fns) == set(gdn_b200.ALGO_ENTRY_POINTS)
     assert gdn_b200.ALGO_NO_DPS <= set(fns)
+
+
+def _flashinfer_parameters(name):
+    """Parameter names and default expressions of a function in the installed
+    flashinfer/gdn_decode.py, read from its source (importing it needs a GPU)."""
+    import ast
+    import importlib.util
+
+    spec = importlib.util.find_spec("flashinfer")
+    if spec is None or not spec.submodule_search_locations:
+        pytest.skip("flashinfer not installed")
+    import os
+
+    path = os.path.join(list(spec.submodule_search_locations)[0], "gdn_decode.py")
+    if not os.path.exists(path):
+        pytest.skip("flashinfer/gdn_decode.py not present")
+    tree = ast.parse(open(path).read())
+    for node in tree.body:
+        if isinstance(node, ast.FunctionDef) and node.name == name:
+            args = node.args.posonlyargs + node.args.args
+            defaults = [None] * (len(args) - len(node.args.defaults)) + [
+                ast.unparse(d) for d in node.args.defaults]
+            return [(a.arg, d) for a, d in zip(args, defaults)]
+    pytest.skip(f"{name} not found in the installed flashinfer")
+
+
+@pytest.mark.parametrize("name", ["gated_delta_rule_decode_pretranspose", "gated_delta_rule_mtp"])
+def test_flashinfer_entry_points_keep_flashinfer_parameters(name):
+    """A caller switching `from flashinfer.gdn_decode import ...` to gdn_b200 passes
+    the same positional and keyword arguments: FlashInfer's parameter list
+    (names, order, defaults) is a prefix of ours; ours only adds optional ones.
+    gated_delta_rule_mtp's disable_state_update defaults to None here (FlashInfer:
+    None as well, treated as True with a warning)."""
+    import inspect
+
+    theirs = _flashinfer_parameters(name)
+    ours = list(inspect.signature(getattr(ops, name)).parameters.values())
+    assert [p.name for p in ours[:len(theirs)]] == [n for n, _ in theirs]
+    for p, (n, default) in zip(ours, theirs):
+        if default is None:
+            assert p.default is inspect.Parameter.empty, n
+        else:
+            assert repr(p.default) == default, (n, p.default, default)
+    for p in ours[len(theirs):]:
+        assert p.default is not inspect.Parameter.empty, p.name
