@@ -51,3 +51,34 @@ def test_tvm_ffi_rejects_bad_dtype(tvm_mod):
     with pytest.raises(Exception, match="output"):
         tvm_mod.kernel_cuda_b200(g.q, g.k, g.v, g.state, g.A_log, g.a, g.dt_bias, g.b, 0.0, out,
                                  g.state)
+
+
+def _parameters(source: str, function: str):
+    """(type, name) pairs of a C++ function definition's parameter list."""
+    import re
+
+    m = re.search(rf"\bvoid\s+{function}\s*\((.*?)\)\s*\{{", source, flags=re.S)
+    assert m, function
+    params = []
+    for p in m.group(1).split(","):
+        p = " ".join(p.replace("tvm::ffi::", "").split())
+        typ, name = p.rsplit(" ", 1)
+        params.append((typ, name))
+    return params
+
+
+def test_export_has_the_reference_signature():
+    """kernel_cuda_b200 takes exactly the reference's KernelCuda parameters (types,
+    order, names; solution/cuda/kernel.cu:216-227), so flashinfer-bench's
+    TVMFFIBuilder calls it like kernel_cuda.  Reads the reference checkout, when
+    present, as text."""
+    ref_root = os.environ.get("GDN_REFERENCE_ROOT", "/root/reference")
+    ref = os.path.join(ref_root, "solution", "cuda", "kernel.cu")
+    if not os.path.exists(ref):
+        pytest.skip("reference checkout not present")
+    ours = os.path.join(os.path.dirname(build.__file__), os.pardir, "csrc", "tvm_ffi_entry.cu")
+    theirs = _parameters(open(ref).read(), "KernelCuda")
+    mine = _parameters(open(ours).read(), "KernelCudaB200")
+    assert len(theirs) == 11
+    assert mine == theirs
+    assert "TVM_FFI_DLL_EXPORT_TYPED_FUNC(kernel_cuda_b200, KernelCudaB200)" in open(ours).read()
