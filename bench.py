@@ -568,6 +568,25 @@ def run_sweep(device):
                               "state_updates_per_s": round(B * HV / (med * 1e-6)),
                               "l2": "flushed" if flush_buf is not None else "inputs > L2"})
         del inp, out
+    # the same step with the in-kernel q/k L2-norm (FlashInfer's use_qk_l2norm=True;
+    # the reference path itself never normalises)
+    res["decode_l2norm"] = []
+    for B in (1, 64, 256):
+        inp = synthetic.make_inputs(B=B, seed=B, device=device)
+        out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
+        flush_buf = l2_flush_buffer(device) if B < 64 else None
+        fn = lambda: gdn_b200.gated_delta_rule_decode_pretranspose(  # noqa: E731
+            inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
+            out, use_qk_l2norm=True)
+        for _ in range(10):
+            fn()
+        med = statistics.median(cupti_kernel_durations_us(
+            fn, 100, device, flush=None if flush_buf is None else flush_buf.zero_))
+        nb = synthetic.bytes_per_call(B)
+        res["decode_l2norm"].append({"B": B, "median_us": round(med, 3),
+                                     "GBps": round(nb / med / 1e3, 1),
+                                     "l2": "flushed" if flush_buf is not None else "inputs > L2"})
+        del inp, out
     # pooled: pool of 1024 slots, 256 active entries drawn as a permutation, one -1
     P, B = 1024, 256
     inp = synthetic.make_inputs(B=B, slots=P, seed=7, device=device)
