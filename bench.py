@@ -518,6 +518,8 @@ def run_b200_arm(args, rank, world, local_rank):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(elapsed_ms_max / K, 5),
+        # (batch entry, v-head) state updates of the whole job per second
+        "state_updates_per_s": round(BATCH * HV * K / (elapsed_ms_max / 1e3)),
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
         "config": dict(workload_config(world), l2=(
