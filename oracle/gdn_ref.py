@@ -17,7 +17,10 @@ Parity pinning: ``tests/golden/make_golden.py`` runs the reference's own
 ``kernel_pt_reference`` and ``kernel_prefill_reference`` (imported from the
 reference checkout) on seeded inputs and stores their outputs under
 ``tests/golden/``; ``tests/test_oracle_golden.py`` checks this module against
-them.
+them.  ``tests/test_oracle_fla_naive.py`` also checks it against an independent
+implementation, flash-linear-attention's naive recurrence (fla 0.5.1,
+fla/ops/gated_delta_rule/naive.py), the package the reference's Triton kernel
+came from.
 
 Per (batch, v-head) with the state viewed as S[K, V] (transpose of the k-last
 storage [V, K]), following kernel.py:73-114:
