@@ -869,12 +869,17 @@ int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float
                   void* stream) {
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return GDN_ERR_ARG;
   if (static_cast<long long>(HV) * world > 0x7fffffffLL / kDim) return GDN_ERR_SHAPE;
-  const int rc = check_common(q, k, v, state, A_log, a, dt_bias, b, peer_outputs, B, 1, H,
+  // this rank's own output buffer is the one its outputs (and the checks) refer to
+  const gdn_bf16* own_out = peer_outputs ? peer_outputs[rank] : nullptr;
+  const int rc = check_common(q, k, v, state, A_log, a, dt_bias, b, own_out, B, 1, H,
                               HV * world, K, V, B);
   if (rc == kNothingToDo) return GDN_OK;
   if (rc != GDN_OK) return rc;
   if (!peer_signals || !status || !epoch_counter) return GDN_ERR_NULL;
   if (!aligned(status, 4) || !aligned(epoch_counter, 4)) return GDN_ERR_ALIGN;
+  const size_t state_bytes = static_cast<size_t>(B) * HV * kHeadElems * sizeof(float);
+  const size_t out_bytes = static_cast<size_t>(B) * HV * world * kDim * sizeof(gdn_bf16);
+  if (overlaps(state, state_bytes, own_out, out_bytes)) return GDN_ERR_ALIAS;
   StepArgs p = make_args(q, k, v, state, state, A_log, a, dt_bias, b, scale, nullptr, B, 1, H, HV,
                          K, B, use_qk_l2norm);
   BarrierArgs bar{};
@@ -926,7 +931,8 @@ std::mutex g_static_mutex;
 uint32_t* g_static_epochs_dev[kMaxDevices];  // device address per device, null until set up
 
 // Device address of g_tp_static_epochs on the current device, looked up (with that
-// device current) on the first call for the device.
+// device current) on the first call for the device and cached for the life of the
+// process (a cudaDeviceReset unloads the module; the header forbids use after one).
 int static_epochs(uint32_t** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return GDN_ERR_LAUNCH;

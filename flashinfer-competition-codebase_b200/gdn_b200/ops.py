@@ -66,7 +66,13 @@ def _resolve_scale(scale, K: int) -> float:
     return float(scale)
 
 
-def _index_tensor(idx: torch.Tensor, name: str, B: int, device) -> torch.Tensor:
+def _index_tensor(idx: torch.Tensor, name: str, B: int, device, pool: int) -> torch.Tensor:
+    """Slot indices as the contiguous int32 tensor the kernels read.
+
+    int64 indices are clamped to [-1, pool] on the device before narrowing, so a
+    value beyond the int32 range cannot wrap onto a valid slot: anything >= pool
+    stays out of range (skipped and counted by the kernel) and anything negative
+    stays negative (the -1 conventions).  No host synchronisation."""
     if not isinstance(idx, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
     if tuple(idx.shape) != (B,):
@@ -75,6 +81,8 @@ def _index_tensor(idx: torch.Tensor, name: str, B: int, device) -> torch.Tensor:
         raise TypeError(f"{name} must be int32 or int64, got {idx.dtype}")
     if idx.device != device:
         raise ValueError(f"{name} is on {idx.device}, expected {device}")
+    if idx.dtype == torch.int64:
+        idx = idx.clamp(min=-1, max=max(int(pool), 0))
     return idx.to(torch.int32).contiguous()
 
 
@@ -196,9 +204,9 @@ def gated_delta_rule_decode_pretranspose(
         return output, state
     pool = initial_state.shape[0] if initial_state.dim() == 4 else -1
     _check(initial_state, "initial_state", _F32, (pool, HV, V, K), dev)
-    idx_in = _index_tensor(initial_state_indices, "initial_state_indices", B, dev)
+    idx_in = _index_tensor(initial_state_indices, "initial_state_indices", B, dev, pool)
     idx_out = (None if output_state_indices is None else
-               _index_tensor(output_state_indices, "output_state_indices", B, dev))
+               _index_tensor(output_state_indices, "output_state_indices", B, dev, pool))
     with torch.cuda.device(dev):
         _lib.call(
             "gdn_decode_pooled",
@@ -227,12 +235,12 @@ def decode_bf16_state(q, k, v, state_pool, A_log, a, dt_bias, b, scale=None, out
     B, T, H, HV, K, V, dev = _check_step_inputs(q, k, v, A_log, a, dt_bias, b)
     pool = state_pool.shape[0] if state_pool.dim() == 4 else -1
     _check(state_pool, "state_pool", _BF16, (pool, HV, V, K), dev)
-    idx = None if state_indices is None else _index_tensor(state_indices, "state_indices", B, dev)
+    idx = None if state_indices is None else _index_tensor(state_indices, "state_indices", B, dev, pool)
     oidx = None
     if output_state_indices is not None:
         if idx is None:
             raise ValueError("output_state_indices needs state_indices")
-        oidx = _index_tensor(output_state_indices, "output_state_indices", B, dev)
+        oidx = _index_tensor(output_state_indices, "output_state_indices", B, dev, pool)
     if idx is None and pool < B:
         raise ValueError(f"state_pool holds {pool} slots; without indices it needs >= B={B}")
     if output is None:
@@ -289,7 +297,7 @@ def gated_delta_rule_mtp(
     _check(initial_state, "initial_state", _F32, (pool, HV, V, K), dev)
     idx = None
     if initial_state_indices is not None:
-        idx = _index_tensor(initial_state_indices, "initial_state_indices", B, dev)
+        idx = _index_tensor(initial_state_indices, "initial_state_indices", B, dev, pool)
     elif pool < B:
         raise ValueError(f"initial_state holds {pool} slots; without indices it needs >= B={B}")
     if output is None:
@@ -326,7 +334,7 @@ def decode_tuned(q, k, v, state_pool, A_log, a, dt_bias, b, scale, output, state
     pool = state_pool.shape[0]
     _check(state_pool, "state_pool", _F32, (pool, HV, V, K), dev)
     _check(output, "output", _BF16, (B, T, HV, V), dev)
-    idx = None if state_indices is None else _index_tensor(state_indices, "state_indices", B, dev)
+    idx = None if state_indices is None else _index_tensor(state_indices, "state_indices", B, dev, pool)
     with torch.cuda.device(dev):
         _lib.call(
             "gdn_decode_tuned",

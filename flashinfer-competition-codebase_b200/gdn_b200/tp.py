@@ -14,8 +14,9 @@ Two ways to do that exchange:
   while the other rows are still being computed, then a one-CTA kernel makes
   the ranks meet at a bounded barrier on signal words (``gdn_decode_tp``).  The buffers are torch symmetric memory with NVLink
   multicast disabled (plain peer pointers only); outputs alternate between two
-  buffers by step parity so a fast rank cannot overwrite rows a slow rank is
-  still reading.
+  buffers by step parity, so a fast rank's next step cannot overwrite rows a slow
+  rank is still reading, provided each rank consumes a step's output before it
+  enqueues its next step (see ``TPDecode.step``).
 * ``collective="nccl"``: the local kernel writes [B, 1, HV/W, V], NCCL
   all-gathers it into a rank-major buffer [W, B, HV/W, V], and the library's
   head-interleave kernel reorders it.  This is the baseline, and the path the
@@ -226,9 +227,13 @@ class TPDecode:
         """Inputs are this rank's shards (``HeadShard.shard_inputs``); the local
         state is updated in place.  Returns the full output [B, 1, HV, V]: with
         ``collective="peer"`` and ``out=None`` that is a view of an internal
-        buffer, valid until the next-but-one step (pass ``out`` to get a copy).
-        ``kernel_events`` = (start, end) CUDA events recorded around the decode
-        launch (for ``"peer"`` the launch includes the exchange)."""
+        buffer, valid only until the next step (or replay) is enqueued on this
+        rank: consume it first (enqueue the work that reads it on the same stream),
+        or pass ``out`` to get a copy.  The two peer buffers alternate, and another
+        rank's step after next writes this buffer as soon as this rank's next
+        barrier has signalled, so a read enqueued after the next step may race with
+        that write.  ``kernel_events`` = (start, end) CUDA events recorded around the
+        decode launch (for ``"peer"`` the launch includes the exchange)."""
         B = q.shape[0]
         if B > self.max_batch:
             raise ValueError(f"batch {B} exceeds max_batch {self.max_batch}")
@@ -269,7 +274,8 @@ class CapturedSteps:
 
     def replay(self) -> torch.Tensor:
         """Run the recorded steps once; returns the last step's output
-        [B, 1, HV, V] (valid until that buffer is written again two steps later)."""
+        [B, 1, HV, V], valid only until the next step or replay is enqueued on this
+        rank (the same rule as ``TPDecode.step``): consume or copy it before that."""
         i = self.tp._steps & 1
         self.graphs[i].replay()
         self.count += 1

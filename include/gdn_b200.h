@@ -228,6 +228,10 @@ GDN_API int gdn_decode_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf1
  *    returns instead of waiting forever, and that output is incomplete.
  *  - Two consecutive calls must not write the same output buffers (a fast rank
  *    could overwrite rows a slow rank is still reading): alternate two buffers.
+ *    With two buffers the output of call n is valid only until this rank
+ *    enqueues call n+1: another rank's call n+2 writes the same buffer as soon
+ *    as this rank's barrier n+1 has signalled, so work that reads output n
+ *    must be enqueued on `stream` before call n+1 (or copy it out first).
  * Every rank must make the same sequence of calls with the same B, H, HV and
  * world.  Enqueues two kernels on `stream`.
  */
@@ -260,6 +264,9 @@ GDN_API int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* 
  *    first call on that channel), and the same channel number on every rank.
  *  - Every call on a channel shares its counter: calls on the same channel
  *    that overlap on the GPU (different streams, no ordering) race.
+ *  - The device address is cached per device ordinal for the life of the
+ *    process.  Do not call this entry after cudaDeviceReset on that device
+ *    (the reset unloads the module and the cached address goes stale).
  * Other arguments and results as gdn_decode_tp.
  */
 GDN_API int gdn_decode_tp_static(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,

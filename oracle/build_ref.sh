@@ -7,11 +7,12 @@
 # (solution/cuda/binding.py:19-28: --use_fast_math via tvm_ffi.cpp.build), with the
 # architecture made explicit for sm_100a because this machine has no GPU to query.
 #
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: $GDN_REFERENCE_ROOT, else the
-# checkout location that __graft_entry__.build() also uses)
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: $GDN_REFERENCE_ROOT; there is
+# no built-in location: __graft_entry__.build() passes the checkout it found)
 set -euo pipefail
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
-REF="${1:-${GDN_REFERENCE_ROOT:-/root/reference}}"
+REF="${1:-${GDN_REFERENCE_ROOT:-}}"
+if [ -z "$REF" ]; then echo "usage: build_ref.sh REFERENCE_ROOT (or set GDN_REFERENCE_ROOT)" >&2; exit 2; fi
 SRC="$REF/solution/cuda/kernel.cu"
 OUT="$HERE/_ref/libref_kernel.so"
 if [ ! -f "$SRC" ]; then echo "reference source not found: $SRC" >&2; exit 2; fi

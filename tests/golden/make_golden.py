@@ -110,9 +110,12 @@ def save(name, meta, **arrays):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("GDN_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("GDN_REFERENCE_ROOT"),
+                    help="reference checkout (default: $GDN_REFERENCE_ROOT)")
     ap.add_argument("--only", default=None, help="comma-separated fixture names to (re)make")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("pass --reference PATH or set GDN_REFERENCE_ROOT")
     ref, prefill_ref = load_reference(args.reference)
     torch.manual_seed(0)
     only = None if args.only is None else set(args.only.split(","))

@@ -152,7 +152,9 @@ def test_tp_rejects(gdn_lib):
     import ctypes
     f = gdn_lib.gdn_decode_tp
     arr = (ctypes.c_void_p * 2)(P, P)
-    base = dict(q=P, k=P, v=P, state=P, A_log=P, a=P, dt_bias=P, b=P, scale=0.0, outs=arr,
+    O = 1 << 30                                   # output buffers, disjoint from the state
+    outs = (ctypes.c_void_p * 2)(O, O)
+    base = dict(q=P, k=P, v=P, state=P, A_log=P, a=P, dt_bias=P, b=P, scale=0.0, outs=outs,
                 sigs=arr, epoch=P, status=P, timeout=0, rank=0, world=2, B=2, H=8,
                 HV=16, K=128, V=128, l2=0, stream=None)
 
@@ -167,6 +169,12 @@ def test_tp_rejects(gdn_lib):
     assert call(epoch=P + 2) == _lib.GDN_ERR_ALIGN
     assert call(sigs=None) == _lib.GDN_ERR_NULL
     assert call(status=None) == _lib.GDN_ERR_NULL
-    assert call(outs=(ctypes.c_void_p * 2)(P, None)) == _lib.GDN_ERR_NULL
-    assert call(outs=(ctypes.c_void_p * 2)(P, P + 8)) == _lib.GDN_ERR_ALIGN
+    assert call(outs=(ctypes.c_void_p * 2)(O, None)) == _lib.GDN_ERR_NULL
+    assert call(outs=(ctypes.c_void_p * 2)(O, O + 8)) == _lib.GDN_ERR_ALIGN
     assert call(K=64) == _lib.GDN_ERR_SHAPE
+    # this rank's own output buffer is the one validated: bf16 alignment, and no
+    # overlap with this rank's state (2 x 8 heads x 64 KiB from P)
+    assert call(outs=(ctypes.c_void_p * 2)(O + 1, O)) == _lib.GDN_ERR_ALIGN
+    assert call(outs=(ctypes.c_void_p * 2)(None, O)) == _lib.GDN_ERR_NULL
+    assert call(outs=(ctypes.c_void_p * 2)(P + 4096, O)) == _lib.GDN_ERR_ALIAS
+    assert call(outs=(ctypes.c_void_p * 2)(O, P + 4096), rank=1) == _lib.GDN_ERR_ALIAS

@@ -49,11 +49,24 @@ def test_pool_argument_rules():
     with pytest.raises(ValueError, match="either state"):
         f(*args[:3], None, *args[4:8])
     with pytest.raises(ValueError, match="shape"):
-        ops._index_tensor(torch.zeros(3, dtype=torch.int32), "idx", 2, torch.device("cpu"))
+        ops._index_tensor(torch.zeros(3, dtype=torch.int32), "idx", 2, torch.device("cpu"), 4)
     with pytest.raises(TypeError, match="int32 or int64"):
-        ops._index_tensor(torch.zeros(2), "idx", 2, torch.device("cpu"))
-    idx = ops._index_tensor(torch.tensor([3, -1]), "idx", 2, torch.device("cpu"))
+        ops._index_tensor(torch.zeros(2), "idx", 2, torch.device("cpu"), 4)
+    idx = ops._index_tensor(torch.tensor([3, -1]), "idx", 2, torch.device("cpu"), 4)
     assert idx.dtype == torch.int32 and idx.tolist() == [3, -1]
+
+
+def test_int64_indices_cannot_wrap_onto_a_valid_slot():
+    """2**32 + 1 would wrap to slot 1 if narrowed to int32; it must stay out of
+    range (>= pool: skipped and counted by the kernel), and a large negative value
+    must stay negative (the -1 conventions)."""
+    big = torch.tensor([2**32 + 1, -(2**40), 2**31, 3, -1, 7], dtype=torch.int64)
+    idx = ops._index_tensor(big, "idx", 6, torch.device("cpu"), 4)
+    assert idx.dtype == torch.int32
+    assert idx.tolist() == [4, -1, 4, 3, -1, 4]
+    same = ops._index_tensor(torch.tensor([0, 3], dtype=torch.int32), "idx", 2,
+                             torch.device("cpu"), 4)
+    assert same.tolist() == [0, 3]
 
 
 def test_scale_default():

@@ -1,20 +1,21 @@
-"""The bindings that INTEGRATION.md tells a maintainer of the reference to add,
+"""The bindings a maintainer of the reference adds to route its decode path here,
 run against the built library on the CPU.
 
 * A plain C99 caller compiled with gcc against include/gdn_b200.h (warnings as
   errors), linked with libgdn_b200.so and run: the header is C, the library
   loads with no CUDA library on the loader path, and argument errors come back
   as codes before any CUDA call.
-* The ctypes stub of INTEGRATION.md section 1 (the replacement for
-  solution/cuda/binding.py's kernel_cuda), executed verbatim apart from the
-  library path: its argtypes agree with the header, and a bad shape raises
-  with the library's own message.
+* The ctypes binding a maintainer copies next to the reference's
+  solution/cuda/binding.py (integration/binding_b200.py, the replacement for
+  its kernel_cuda), imported as is with the library path in GDN_B200_LIB: its
+  argtypes agree with the header, and a bad shape raises with the library's
+  own message.
 
 Every call here fails validation or is a B = 0 no-op, so no GPU is needed.
 """
 
+import importlib.util
 import os
-import re
 import shutil
 import subprocess
 import types
@@ -26,7 +27,8 @@ from gdn_b200 import _lib
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 INCLUDE = os.path.join(ROOT, "include")
-INTEGRATION = os.path.join(ROOT, "INTEGRATION.md")
+BINDING = os.path.join(ROOT, "flashinfer-competition-codebase_b200", "integration",
+                       "binding_b200.py")
 
 C_CALLER = r"""
 #include <stdio.h>
@@ -76,20 +78,17 @@ def test_plain_c_caller_compiles_links_and_runs(gdn_lib, tmp_path):
     assert run.stdout.strip() == "ok"
 
 
-def _ctypes_stub_source() -> str:
-    text = open(INTEGRATION).read()
-    section = text.split("## 1. ", 1)[1].split("\n## ", 1)[0]
-    blocks = re.findall(r"```python\n(.*?)```", section, flags=re.S)
-    stub = [b for b in blocks if "def kernel_cuda_b200" in b]
-    assert len(stub) == 1
-    return stub[0]
+def _load_binding(lib_path, monkeypatch):
+    monkeypatch.setenv("GDN_B200_LIB", lib_path)
+    spec = importlib.util.spec_from_file_location("binding_b200", BINDING)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
 
 
-def test_integration_ctypes_stub_matches_the_header(gdn_lib, monkeypatch):
-    code = _ctypes_stub_source().replace("/path/to/libgdn_b200.so", gdn_lib._name)
-    ns: dict = {}
-    exec(compile(code, "INTEGRATION.md#1", "exec"), ns)
-    stub_lib = ns["_lib"]
+def test_integration_ctypes_binding_matches_the_header(gdn_lib, monkeypatch):
+    binding = _load_binding(gdn_lib._name, monkeypatch)
+    stub_lib = binding._lib
     restype, argtypes = _lib.SIGNATURES["gdn_decode"]
     assert stub_lib.gdn_decode.restype is restype
     assert list(stub_lib.gdn_decode.argtypes) == argtypes
@@ -109,4 +108,4 @@ def test_integration_ctypes_stub_matches_the_header(gdn_lib, monkeypatch):
     b = torch.zeros(B, 1, HV, dtype=bf)
     out = torch.empty(B, 1, HV, V, dtype=bf)
     with pytest.raises(RuntimeError, match="K and V must be 128"):
-        ns["kernel_cuda_b200"](q, k, v, state, A_log, a, dt_bias, b, None, out, state)
+        binding.kernel_cuda_b200(q, k, v, state, A_log, a, dt_bias, b, None, out, state)

@@ -72,10 +72,12 @@ def test_export_has_the_reference_signature():
     order, names; solution/cuda/kernel.cu:216-227), so flashinfer-bench's
     TVMFFIBuilder calls it like kernel_cuda.  Reads the reference checkout, when
     present, as text."""
-    ref_root = os.environ.get("GDN_REFERENCE_ROOT", "/root/reference")
+    import __graft_entry__
+
+    ref_root = __graft_entry__.reference_root()
+    if ref_root is None:
+        pytest.skip("reference checkout not present (GDN_REFERENCE_ROOT)")
     ref = os.path.join(ref_root, "solution", "cuda", "kernel.cu")
-    if not os.path.exists(ref):
-        pytest.skip("reference checkout not present")
     ours = os.path.join(os.path.dirname(build.__file__), os.pardir, "csrc", "tvm_ffi_entry.cu")
     theirs = _parameters(open(ref).read(), "KernelCuda")
     mine = _parameters(open(ours).read(), "KernelCudaB200")
