@@ -6,18 +6,33 @@ layer at batch 256 — 16 q/k heads, 32 v-heads, K = V = 128, T = 1 — with the
 fp32 state [256, 32, 128, 128] (512 MiB) updated in place in HBM.  With
 ``--gpus N`` (torchrun, one process per GPU) the 32 v-heads and their 16 q/k
 heads are split across the N ranks (tensor parallel, total work fixed) and
-the bf16 outputs are all-gathered over NVLink by NCCL and head-interleaved.
+every rank ends the step with the full bf16 output.
 
 value   algorithmic HBM bytes of the whole job per second (GB/s): 4,219,008 B
         per batch entry + 256 B per call, times steps, over the device time of
         the timed steps (CUDA events, max over ranks).  Inputs are resident
-        in HBM; the 512 MiB state exceeds the 126 MB L2, so no flush is needed.
-e2e     the same metric through the public API (``kernel_cuda_b200`` / the TP
-        step) with the per-step inputs (q, k, v, a, b) copied from pinned host
-        memory and the output read back to the host inside the timed region.
+        in HBM and larger than L2 (several layers' states updated round robin).
+e2e     the same metric through the public API (``kernel_cuda_b200``; at N > 1
+        the captured ``TPDecode`` step) with every step's inputs (q, k, v, a, b)
+        copied from pinned host memory and its output read back to pinned host
+        memory inside the timed region.  Copies run on their own streams, double
+        buffered, so step i's kernel overlaps the upload of step i+1 and the
+        read-back of step i-1 (ordered by CUDA events).
+parity  before timing, one eager step and one replayed CUDA-graph step on the same
+        seeded inputs (drawn identically on every rank and split by heads at N > 1)
+        are compared with the CPU oracle on sampled batch entries: the gathered
+        output on rank 0, each rank's own state shard.  A mismatch makes the run
+        exit non-zero.
+configs BASELINE's other single-GPU configurations at reduced iterations (N = 1):
+        the batch sweep B in {1,8,32,64,128,256}, the 1024-slot pool with 256
+        entries, T in {2,4} at B = 64 with intermediates, the bf16-stored state
+        and the in-kernel q/k L2-norm; CUPTI medians, algorithmic GB/s, fraction of
+        the measured copy peak.
 latency_b1_us   the B=1 decode kernel's median device duration from CUPTI
-        activity records (torch.profiler), L2 flushed before every launch.
-roofline        the decode kernel alone (CUDA events around each launch).
+        activity records (torch.profiler), L2 flushed before every launch, next to
+        the floor of the method: this repository's own in-place state round trip
+        with the decode kernel's grid and cache hints, same flush.
+roofline        the decode kernel alone (CUDA events around the graph of steps).
 cpu_baseline    the reference's CPU algorithm (oracle restatement of
         kernel_pt_reference, its per-head loop) on a bounded sample, host cores.
 
@@ -25,13 +40,13 @@ At N > 1 the output exchange is fused into the decode kernel (each rank stores i
 rows into every rank's buffer over NVLink, then a bounded barrier); ``--tp-collective
 nccl`` uses NCCL all-gather + the interleave kernel instead.
 ``--impl reference`` times that CPU implementation alone as the reference arm.
-``--sweep PATH`` also writes a batch sweep (B in 1..256, plus the pooled and
-multi-token configurations) as JSON to PATH.
+``--profile-case B`` runs a few launches of one small decode case and exits (for ncu).
 """
 
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -55,7 +70,11 @@ METRIC = "GDN decode µs (CUPTI) at B=1; state-update HBM GB/s vs peak at B=256"
 UNIT = "GB/s"
 BATCH, H, HV, DIM = 256, 16, 32, 128
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+B200_L2_BYTES = 126 * 1024 * 1024     # used only where no GPU can be queried
 PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "gdn_step_kernel_b256.txt")
+OUT_TOL = dict(atol=1e-2, rtol=1e-2)      # bf16 output (north star)
+STATE_TOL = dict(atol=1e-3, rtol=1e-3)    # fp32 state (north star)
+PARITY_ENTRIES = (0, 85, 170, 255)        # sampled batch entries checked against the oracle
 
 # NVML clock-event reason bits
 _REASONS = {
@@ -215,6 +234,32 @@ def max_over_ranks(x: float, world: int, device) -> float:
     return float(t.item())
 
 
+def l2_size_bytes() -> int:
+    if torch.cuda.is_available():
+        return int(torch.cuda.get_device_properties(0).L2_cache_size)
+    return B200_L2_BYTES
+
+
+def layer_count(world: int, l2_bytes: int):
+    """Layers whose per-GPU states together hold >= 3x the L2, and one layer's bytes."""
+    state_bytes = BATCH * (HV // world) * DIM * DIM * 4
+    return max(1, math.ceil(3 * l2_bytes / state_bytes)), state_bytes
+
+
+def workload_config(world, l2_bytes):
+    """The workload, identical in both arms' lines."""
+    layers, state_bytes = layer_count(world, l2_bytes)
+    return {
+        "workload": "gdn_decode_qwen3next_b256_t1",
+        "global_batch": BATCH, "T": 1, "num_qk_heads": H, "num_v_heads": HV, "head_dim": DIM,
+        "state": "fp32 [256,32,128,128] k-last, updated in place",
+        "parallelism": f"tp{world}",
+        "l2": (f"inputs larger than L2, no flush: {layers} layer state(s) of "
+               f"{state_bytes >> 20} MiB per GPU updated round robin "
+               f"({(layers * state_bytes) >> 20} MiB >= 3x the {l2_bytes >> 20} MiB L2)"),
+    }
+
+
 # ---------------------------------------------------------------------------
 # CPU leg: the reference's algorithm on the host cores
 # ---------------------------------------------------------------------------
@@ -278,7 +323,7 @@ def run_reference_arm(args, rank, world):
         "ms_per_step": round(1e3 * total / len(times), 3),
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(world),
+        "config": workload_config(world, l2_size_bytes()),
         "cpu_baseline": {"value": round(gbs, 6), "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(gbs, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -291,13 +336,15 @@ def run_reference_arm(args, rank, world):
 # GPU leg
 # ---------------------------------------------------------------------------
 
-def workload_config(world):
-    return {
-        "workload": "gdn_decode_qwen3next_b256_t1",
-        "global_batch": BATCH, "T": 1, "num_qk_heads": H, "num_v_heads": HV, "head_dim": DIM,
-        "state": "fp32 [256,32,128,128] k-last, updated in place",
-        "parallelism": f"tp{world}",
-    }
+def _probe_lib():
+    from gdn_b200 import build
+
+    if not os.path.exists(build.PROBE_LIB_PATH):
+        raise RuntimeError(f"{build.PROBE_LIB_PATH} missing: run __graft_entry__.build()")
+    lib = ctypes.CDLL(build.PROBE_LIB_PATH)
+    lib.gdn_probe_state_roundtrip.restype = ctypes.c_int
+    lib.gdn_probe_state_roundtrip.argtypes = [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p]
+    return lib
 
 
 def b1_latency(device, iters=200):
@@ -315,11 +362,22 @@ def b1_latency(device, iters=200):
         fn()
     d = cupti_kernel_durations_us(fn, iters, device, flush=flush_buf.zero_)
     d_warm = cupti_kernel_durations_us(fn, iters, device, flush=None)
-    # floor of the method: the same 2 MiB state read and written in place by a plain
-    # elementwise kernel (torch mul_), same flush, same CUPTI records
+    # floor of the method: this repository's own kernel that reads and writes the same
+    # 2 MiB state in place with the decode kernel's grid, work split and cache hints
+    # but no math, same flush, same CUPTI records
+    probe = _probe_lib()
     scratch = inp.state.clone()
-    floor = cupti_kernel_durations_us(lambda: scratch.mul_(1.0), iters, device,
-                                      name="MulFunctor", flush=flush_buf.zero_)
+    stream = torch.cuda.current_stream(device).cuda_stream
+
+    def floor_fn():
+        rc = probe.gdn_probe_state_roundtrip(scratch.data_ptr(), HV, stream)
+        if rc != 0:
+            raise RuntimeError(f"gdn_probe_state_roundtrip failed ({rc})")
+
+    for _ in range(20):
+        floor_fn()
+    floor = cupti_kernel_durations_us(floor_fn, iters, device, name="roundtrip_kernel",
+                                      flush=flush_buf.zero_)
     res = {"median_us": None, "source": "cupti (torch.profiler activity records)",
            "l2": "flushed before every launch (256 MiB write)", "iters": len(d)}
     if d:
@@ -330,19 +388,10 @@ def b1_latency(device, iters=200):
         res["median_us_l2_warm"] = round(statistics.median(d_warm), 3)
     if floor:
         res["copy_floor_us"] = round(statistics.median(floor), 3)
-        res["copy_floor"] = "torch in-place mul_ of the same 2 MiB state, L2 flushed, CUPTI"
+        res["copy_floor"] = ("gdn_probe_state_roundtrip: in-place read+write of the same 2 MiB "
+                             "state, decode kernel's grid (256 CTAs x 128 threads) and cache "
+                             "hints, no math; L2 flushed; CUPTI")
     return res
-
-
-def sanity_check(state, device, step_fn):
-    """Runs the first step and checks, without any reference, that every output
-    element is finite and that the state changed (parity with the reference is
-    the GPU tests' job)."""
-    before = state[:2].clone()
-    out = step_fn()
-    torch.cuda.synchronize(device)
-    return {"outputs_finite": bool(torch.isfinite(out.float()).all()),
-            "state_updated": bool(not torch.equal(before, state[:2]))}
 
 
 class _PlainGraph:
@@ -366,10 +415,61 @@ class _PlainGraph:
         return self.out
 
 
+def _compare(got, want, tol):
+    got, want = got.float(), want.float()
+    err = (got - want).abs()
+    bound = tol["atol"] + tol["rtol"] * want.abs()
+    return float(err.max()), bool((err <= bound).all())
+
+
+def _e2e_pipeline(device, world, rank, steps, host_in, dev_in, states, run_step, dev_out,
+                  host_out, out_rows):
+    """``steps`` steps end to end, timed with CUDA events on the launching stream.
+
+    Step i uses device input buffer j = i % 2: its H2D copy (side stream) waits until
+    step i-2's kernel has read that buffer; the step waits for its H2D; the step's
+    output rows are read back (side stream) into pinned host memory, and step i+2
+    waits for that read before it writes device output buffer j again.
+    ``run_step(i, j)`` enqueues the step on the current stream and returns the tensor
+    holding this rank's output rows for step i (already in dev_out[j])."""
+    compute = torch.cuda.current_stream(device)
+    s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev_h2d = [torch.cuda.Event() for _ in range(2)]
+    ev_kern = [torch.cuda.Event() for _ in range(2)]
+    ev_d2h = [torch.cuda.Event() for _ in range(2)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(compute)
+    s_h2d.wait_stream(compute)
+    s_d2h.wait_stream(compute)
+    for i in range(steps):
+        j = i & 1
+        with torch.cuda.stream(s_h2d):
+            if i >= 2:
+                s_h2d.wait_event(ev_kern[j])
+            for name, t in host_in.items():
+                dev_in[j][name].copy_(t, non_blocking=True)
+            ev_h2d[j].record(s_h2d)
+        compute.wait_event(ev_h2d[j])
+        if i >= 2:
+            compute.wait_event(ev_d2h[j])
+        run_step(i, j)
+        ev_kern[j].record(compute)
+        with torch.cuda.stream(s_d2h):
+            s_d2h.wait_event(ev_kern[j])
+            host_out[j].copy_(dev_out[j], non_blocking=True)
+            ev_d2h[j].record(s_d2h)
+    compute.wait_stream(s_d2h)
+    compute.wait_stream(s_h2d)
+    e1.record(compute)
+    torch.cuda.synchronize(device)
+    return e0.elapsed_time(e1)
+
+
 def run_b200_arm(args, rank, world, local_rank):
     import gdn_b200
     from gdn_b200 import synthetic
     from gdn_b200.tp import HeadShard, TPDecode
+    from oracle import gdn_ref      # the parity checker only; nothing timed calls it
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
@@ -381,25 +481,36 @@ def run_b200_arm(args, rank, world, local_rank):
     shard = HeadShard(rank, world, H, HV)
     hl, hvl = shard.h_local, shard.hv_local
 
-    # Local shard inputs, drawn on the device.  Each step updates one "layer's"
-    # state and the next step the next layer's (round robin), like the GDN layers of
-    # a model: with enough layers the per-GPU working set stays >= 3x the L2, so no
-    # step finds its state cached by the previous one (at N=8 one layer's shard is
-    # only 64 MiB).  q/k/v/a/b are shared by the layers.
-    inp = synthetic.make_inputs(B=BATCH, H=hl, HV=hvl, seed=1234 + rank, device=device)
-    l2_bytes = torch.cuda.get_device_properties(device).L2_cache_size
-    state_bytes = inp.state.numel() * inp.state.element_size()
-    layers = max(1, math.ceil(3 * l2_bytes / state_bytes))
+    # One set of full inputs drawn on the device from one seed, identical on every rank
+    # (same generator, same device type), then cut into this rank's head shard.  The
+    # sampled entries' inputs go to the host for the oracle before the state changes.
+    full = synthetic.make_inputs(B=BATCH, seed=1234, device=device)
+    sel = torch.tensor(PARITY_ENTRIES, device=device)
+    ref_in = dict(q=full.q[sel].cpu(), k=full.k[sel].cpu(), v=full.v[sel].cpu(),
+                  state=full.state[sel].cpu(), A_log=full.A_log.cpu(), a=full.a[sel].cpu(),
+                  dt_bias=full.dt_bias.cpu(), b=full.b[sel].cpu())
+    q, k, v, state0, A_log, a, dt_bias, b = shard.shard_inputs(
+        full.q, full.k, full.v, full.state, full.A_log, full.a, full.dt_bias, full.b)
+    scale = full.scale
+    del full
+    torch.cuda.empty_cache()
+
+    # Each step updates one "layer's" state and the next step the next layer's (round
+    # robin), like the GDN layers of a model: with enough layers the per-GPU working set
+    # stays >= 3x the L2, so no step finds its state cached by the previous one (at N=8
+    # one layer's shard is only 64 MiB).  q/k/v/a/b are shared by the layers.
+    l2_bytes = l2_size_bytes()
+    layers, state_bytes = layer_count(world, l2_bytes)
     gen = torch.Generator(device=device).manual_seed(99 + rank)
-    states = [inp.state] + [torch.randn(inp.state.shape, generator=gen, device=device).mul_(0.1)
-                            for _ in range(layers - 1)]
+    states = [state0] + [torch.randn(state0.shape, generator=gen, device=device).mul_(0.1)
+                         for _ in range(layers - 1)]
     out = torch.empty((BATCH, 1, HV, DIM), dtype=torch.bfloat16, device=device)
     tp = (TPDecode(H=H, HV=HV, max_batch=BATCH, device=device, collective=args.tp_collective)
           if world > 1 else None)
 
-    def layer_args(i):
-        return (inp.q, inp.k, inp.v, states[i % layers], inp.A_log, inp.a, inp.dt_bias, inp.b,
-                inp.scale)
+    def layer_args(i, inputs=None):
+        qq, kk, vv, aa, bb = inputs if inputs is not None else (q, k, v, a, b)
+        return (qq, kk, vv, states[i % layers], A_log, aa, dt_bias, bb, scale)
 
     def eager_step(i):
         """One step of layer i through the public API."""
@@ -408,6 +519,33 @@ def run_b200_arm(args, rank, world, local_rank):
         gdn_b200.kernel_cuda_b200(*layer_args(i), out, states[i % layers])
         return out
 
+    # ---- parity: one eager step, then one replayed CUDA-graph step, on layer 0 ----
+    par_graph = tp.capture(*layer_args(0)) if tp is not None else \
+        _PlainGraph(device, [layer_args(0)], out)
+    got_out = [eager_step(0)[sel].cpu()]        # consumed before the next step is enqueued
+    got_out.append(par_graph.replay()[sel].cpu())
+    got_state = states[0][sel].cpu()
+    del par_graph
+    want_o1, want_s1 = gdn_ref.decode(ref_in["q"], ref_in["k"], ref_in["v"], ref_in["state"],
+                                      ref_in["A_log"], ref_in["a"], ref_in["dt_bias"],
+                                      ref_in["b"], scale)
+    want_o2, want_s2 = gdn_ref.decode(ref_in["q"], ref_in["k"], ref_in["v"], want_s1,
+                                      ref_in["A_log"], ref_in["a"], ref_in["dt_bias"],
+                                      ref_in["b"], scale)
+    e_o1, ok_o1 = _compare(got_out[0], want_o1, OUT_TOL)
+    e_o2, ok_o2 = _compare(got_out[1], want_o2, OUT_TOL)
+    e_s, ok_s = _compare(got_state, want_s2[:, shard.hv0:shard.hv1], STATE_TOL)
+    par = torch.tensor([max(e_o1, e_o2), e_s, 0.0 if (ok_o1 and ok_o2 and ok_s) else 1.0],
+                       dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(par, op=torch.distributed.ReduceOp.MAX)
+    parity = {"entries": list(PARITY_ENTRIES), "steps": ["eager", "graph replay"],
+              "checked": ("gathered output [entries, 1, 32, 128] on every rank; each rank's "
+                          "state shard after both steps"),
+              "max_err_out": float(par[0]), "max_err_state": float(par[1]),
+              "tol": {"out": OUT_TOL, "state": STATE_TOL}, "ok": bool(par[2] == 0.0),
+              "oracle": "oracle.gdn_ref.decode (CPU fp32), same seeded inputs"}
+
     # The timed region is one CUDA graph of all K steps (layer i % layers at step i),
     # as a model's decode graph holds all its layers: no host work and no graph
     # boundaries inside it (separate replays of short graphs left 40-60 us idle
@@ -415,17 +553,8 @@ def run_b200_arm(args, rank, world, local_rank):
     K = args.steps
     seq = [layer_args(i) for i in range(K)]
     graph = tp.capture_sequence(seq) if tp is not None else _PlainGraph(device, seq, out)
-
-    step_no = [0]
-
-    def step():
-        res = eager_step(step_no[0])
-        step_no[0] += 1
-        return res
-
-    sanity = sanity_check(states[0], device, step)
-    for _ in range(args.warmup):
-        step()
+    for i in range(args.warmup):
+        eager_step(i)
     graph.replay()                                        # upload + warm the graph, untimed
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
@@ -454,44 +583,56 @@ def run_b200_arm(args, rank, world, local_rank):
     elapsed_ms = t_start.elapsed_time(t_end)
     kernel_ms = elapsed_ms / K          # steps run back to back inside the graph
     elapsed_ms_max = max_over_ranks(elapsed_ms, world, device)
+    del graph
 
     total_bytes = synthetic.bytes_per_call(BATCH)            # whole job, all heads
     local_bytes = synthetic.bytes_per_call(BATCH, H=hl, HV=hvl)
     value = total_bytes * K / (elapsed_ms_max / 1e3) / 1e9
 
-    # end to end through the public API, host buffers in pinned memory
-    host = {n: getattr(inp, n).cpu().pin_memory() for n in ("q", "k", "v", "a", "b")}
-    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = out_host.numel() * out_host.element_size()
+    # ---- end to end through the public API, host buffers in pinned memory ----
+    names = ("q", "k", "v", "a", "b")
+    local_in = dict(q=q, k=k, v=v, a=a, b=b)
+    host_in = {n: local_in[n].cpu().pin_memory() for n in names}
+    dev_in = [{n: torch.empty_like(local_in[n]) for n in names} for _ in range(2)]
+    rows = BATCH // world                       # this rank reads back its batch rows
+    r0 = rank * rows
+    dev_out = [torch.empty((rows, 1, HV, DIM), dtype=torch.bfloat16, device=device)
+               for _ in range(2)]
+    host_out = [torch.empty(dev_out[0].shape, dtype=torch.bfloat16).pin_memory()
+                for _ in range(2)]
+    h2d_rank = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h_rank = host_out[0].numel() * host_out[0].element_size()
+    if tp is None:
+        def run_step(i, j):
+            gdn_b200.kernel_cuda_b200(*layer_args(i, [dev_in[j][n] for n in names]),
+                                      dev_out[j], states[i % layers])
+        api = "gdn_b200.kernel_cuda_b200 (one call per step)"
+        e2e_graphs = []
+    else:
+        # one captured step per (input buffer, layer) pair that the schedule visits
+        period = 2 * layers // math.gcd(2, layers)
+        e2e_graphs = [tp.capture(*layer_args(i, [dev_in[i & 1][n] for n in names]))
+                      for i in range(period)]
+
+        def run_step(i, j):
+            res = e2e_graphs[i % period].replay()
+            dev_out[j].copy_(res[r0:r0 + rows])    # consume before the next step (buffer rule)
+        api = ("gdn_b200.tp.TPDecode.capture (one captured step replayed per step), each "
+               "rank reading back its batch rows of the gathered output")
     K_e2e = max(1, min(K, 500))
-
-    def e2e_step():
-        for n, t in host.items():
-            getattr(inp, n).copy_(t, non_blocking=True)
-        res = step()                       # public API call, next layer's state
-        out_host.copy_(res, non_blocking=True)
-
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize(device)
+    _e2e_pipeline(device, world, rank, 4, host_in, dev_in, states, run_step, dev_out,
+                  host_out, rows)                                   # warm-up, untimed
     if world > 1:
         torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(K_e2e):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize(device)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world, device)
+    e2e_ms = _e2e_pipeline(device, world, rank, K_e2e, host_in, dev_in, states, run_step,
+                           dev_out, host_out, rows)
+    e2e_ms = max_over_ranks(e2e_ms, world, device)
     e2e_value = total_bytes * K_e2e / (e2e_ms / 1e3) / 1e9
+    del e2e_graphs
 
     latency = b1_latency(device) if (world == 1 and not args.skip_b1) else None
-    sweep = None
-    if args.sweep and world == 1:
-        sweep = run_sweep(device)
-        with open(args.sweep, "w") as f:
-            json.dump(sweep, f, indent=1)
+    configs = run_configs(device, args.config_iters) if (world == 1 and not args.skip_configs) \
+        else None
 
     cpu = None
     if world == 1 and rank == 0 and not args.skip_cpu:
@@ -505,9 +646,11 @@ def run_b200_arm(args, rank, world, local_rank):
         if tp.collective == "peer":
             tp.check()
         torch.distributed.barrier()
-        del graph, tp
+        del tp
         torch.distributed.destroy_process_group()
     if rank != 0:
+        if not parity["ok"]:
+            sys.exit(1)
         return
 
     peaks = load_peaks()
@@ -522,19 +665,20 @@ def run_b200_arm(args, rank, world, local_rank):
         "state_updates_per_s": round(BATCH * HV * K / (elapsed_ms_max / 1e3)),
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
-        "config": dict(workload_config(world), l2=(
-            f"inputs larger than L2, no flush: {layers} layer state(s) of {state_bytes >> 20} MiB "
-            f"per GPU updated round robin ({(layers * state_bytes) >> 20} MiB >= 3x the "
-            f"{l2_bytes >> 20} MiB L2)"), timed_loop=f"one CUDA graph of the {K} steps"),
+        "config": workload_config(world, l2_bytes),
+        "timed_loop": f"one CUDA graph of the {K} steps",
+        "parity": parity,
         "latency_b1_us": latency,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                      "traffic": traffic, "peak_source": peaks["source"],
                      "kernel": "gdn_step_kernel", "kernel_us": round(kernel_ms * 1e3, 2),
                      "algorithmic_bytes_per_launch": local_bytes},
-        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": K_e2e, "api": "gdn_b200.kernel_cuda_b200"
-                if world == 1 else "gdn_b200.tp.TPDecode.step (eager, one call per step)"},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                "h2d_bytes_per_step": h2d_rank * world, "d2h_bytes_per_step": d2h_rank * world,
+                "per_rank": {"h2d": h2d_rank, "d2h": d2h_rank}, "steps": K_e2e, "api": api,
+                "overlap": "H2D / D2H on side streams, double-buffered, ordered by CUDA events",
+                "frac_of_value": round(e2e_value / value, 3)},
         "tp_exchange": None if world == 1 else (
             "fused: decode kernel stores outputs into every rank's buffer over NVLink, "
             "then a one-CTA barrier kernel (roofline.kernel_us covers both); CUDA graphs"
@@ -542,52 +686,59 @@ def run_b200_arm(args, rank, world, local_rank):
             "NCCL all_gather_into_tensor + interleave kernel; CUDA graphs"),
         "gpu_launches": launches_per_step * K,
         "clocks": clocks,
+        "configs": configs,
         "cpu_baseline": cpu,
-        "sanity": sanity,
         "wall_s_timed": round(wall, 4),
     }
     print(json.dumps(line), flush=True)
+    if not parity["ok"]:
+        log(f"[bench] PARITY FAILED: {parity}")
+        sys.exit(1)
 
 
-def run_sweep(device):
-    """Batch sweep and the pooled / multi-token configurations (1 GPU)."""
+def run_configs(device, iters):
+    """BASELINE's single-GPU configurations 2-4 (plus the bf16-stored state and the
+    in-kernel q/k L2-norm) at reduced iterations: CUPTI median per call, algorithmic
+    GB/s and fraction of the measured copy peak.  Small cases (whose state fits in L2)
+    flush L2 before every launch; large ones exceed it."""
     import gdn_b200
     from gdn_b200 import synthetic
 
-    res = {"decode": [], "pooled": None, "mtp": []}
+    peak = load_peaks()["hbm_gbs"]
+    flush_buf = l2_flush_buffer(device)
+    l2 = l2_size_bytes()
+
+    def measure(fn, nbytes, state_bytes, extra):
+        for _ in range(5):
+            fn()
+        flushed = state_bytes < 2 * l2
+        d = cupti_kernel_durations_us(fn, iters, device,
+                                      flush=flush_buf.zero_ if flushed else None)
+        med = statistics.median(d)
+        gbs = nbytes / med / 1e3
+        return dict(extra, median_us=round(med, 3), GBps=round(gbs, 1),
+                    frac=round(gbs / peak, 4), l2="flushed" if flushed else "inputs > 2x L2")
+
+    res = {"peak_gbs": peak, "iters": iters, "decode_batch_sweep": [], "decode_l2norm": [],
+           "bf16_state": [], "mtp": []}
     for B in (1, 8, 32, 64, 128, 256):
         inp = synthetic.make_inputs(B=B, seed=B, device=device)
         out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
-        flush_buf = l2_flush_buffer(device) if B < 64 else None
         fn = lambda: gdn_b200.kernel_cuda_b200(*inp.args(), out, inp.state)  # noqa: E731
-        for _ in range(10):
-            fn()
-        d = cupti_kernel_durations_us(fn, 100, device,
-                                      flush=None if flush_buf is None else flush_buf.zero_)
-        med = statistics.median(d)
-        nb = synthetic.bytes_per_call(B)
-        res["decode"].append({"B": B, "median_us": round(med, 3), "GBps": round(nb / med / 1e3, 1),
-                              "state_updates_per_s": round(B * HV / (med * 1e-6)),
-                              "l2": "flushed" if flush_buf is not None else "inputs > L2"})
+        r = measure(fn, synthetic.bytes_per_call(B), inp.state.numel() * 4, {"B": B})
+        r["state_updates_per_s"] = round(B * HV / (r["median_us"] * 1e-6))
+        res["decode_batch_sweep"].append(r)
         del inp, out
     # the same step with the in-kernel q/k L2-norm (FlashInfer's use_qk_l2norm=True;
     # the reference path itself never normalises)
-    res["decode_l2norm"] = []
     for B in (1, 64, 256):
         inp = synthetic.make_inputs(B=B, seed=B, device=device)
         out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
-        flush_buf = l2_flush_buffer(device) if B < 64 else None
         fn = lambda: gdn_b200.gated_delta_rule_decode_pretranspose(  # noqa: E731
             inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale,
             out, use_qk_l2norm=True)
-        for _ in range(10):
-            fn()
-        med = statistics.median(cupti_kernel_durations_us(
-            fn, 100, device, flush=None if flush_buf is None else flush_buf.zero_))
-        nb = synthetic.bytes_per_call(B)
-        res["decode_l2norm"].append({"B": B, "median_us": round(med, 3),
-                                     "GBps": round(nb / med / 1e3, 1),
-                                     "l2": "flushed" if flush_buf is not None else "inputs > L2"})
+        res["decode_l2norm"].append(measure(fn, synthetic.bytes_per_call(B),
+                                            inp.state.numel() * 4, {"B": B}))
         del inp, out
     # pooled: pool of 1024 slots, 256 active entries drawn as a permutation, one -1
     P, B = 1024, 256
@@ -597,31 +748,20 @@ def run_sweep(device):
     fn = lambda: gdn_b200.gated_delta_rule_decode_pretranspose(  # noqa: E731
         inp.q, inp.k, inp.v, None, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale, out,
         use_qk_l2norm=False, initial_state=inp.state, initial_state_indices=idx)
-    for _ in range(10):
-        fn()
-    med = statistics.median(cupti_kernel_durations_us(fn, 50, device))
-    nb = synthetic.bytes_per_call(B, active=B - 1)
-    res["pooled"] = {"pool": P, "B": B, "active": B - 1, "median_us": round(med, 3),
-                     "GBps": round(nb / med / 1e3, 1)}
-    del inp, out
+    res["pooled"] = measure(fn, synthetic.bytes_per_call(B, active=B - 1),
+                            inp.state.numel() * 4, {"pool": P, "B": B, "active": B - 1})
+    del inp, out, idx
     # bf16-stored state (FlashInfer's bf16-state backend): half the state bytes
-    res["bf16_state"] = []
-    for B, flushed in ((1, True), (64, False), (256, False)):
+    for B in (1, 64, 256):
         inp = synthetic.make_inputs(B=B, seed=B, device=device)
         inp.state = inp.state.to(torch.bfloat16)
         out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
-        flush_buf = l2_flush_buffer(device) if flushed else None
         fn = lambda: gdn_b200.decode_bf16_state(  # noqa: E731
             inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b, inp.scale, out)
-        for _ in range(10):
-            fn()
-        med = statistics.median(cupti_kernel_durations_us(
-            fn, 100 if flushed else 50, device, flush=None if flush_buf is None else flush_buf.zero_))
-        nb = synthetic.bytes_per_call(B, state_elem_bytes=2)
-        res["bf16_state"].append({"B": B, "median_us": round(med, 3),
-                                  "GBps": round(nb / med / 1e3, 1),
-                                  "l2": "flushed" if flushed else "inputs > L2"})
+        res["bf16_state"].append(measure(fn, synthetic.bytes_per_call(B, state_elem_bytes=2),
+                                         inp.state.numel() * 2, {"B": B}))
         del inp, out
+    # multi-token speculative verify, B = 64, one intermediate state per token
     for T in (2, 4):
         B = 64
         inp = synthetic.make_inputs(B=B, T=T, seed=T, device=device)
@@ -630,14 +770,224 @@ def run_sweep(device):
         fn = lambda: gdn_b200.gated_delta_rule_mtp(  # noqa: E731
             inp.q, inp.k, inp.v, inp.state, None, inp.A_log, inp.a, inp.dt_bias, inp.b,
             inp.scale, out, inter, disable_state_update=False, use_qk_l2norm=False)
-        for _ in range(5):
-            fn()
-        med = statistics.median(cupti_kernel_durations_us(fn, 50, device))
-        nb = synthetic.bytes_per_call(B, T=T, intermediates=True)
-        res["mtp"].append({"B": B, "T": T, "median_us": round(med, 3),
-                           "GBps": round(nb / med / 1e3, 1)})
+        res["mtp"].append(measure(fn, synthetic.bytes_per_call(B, T=T, intermediates=True),
+                                  (T + 1) * inp.state.numel() * 4, {"B": B, "T": T}))
         del inp, out, inter
     return res
+
+
+def run_compare(device, iters, path):
+    """Same-GPU head-to-head with the kernels the reference measures against, on one
+    GPU with local tensors only: FlashInfer's CuTe-DSL decode (fp32 state, exactly as
+    the reference's kernel_fi_baseline calls it, solution/triton/kernel.py:124-147;
+    and its bf16-state and multi-token paths) and flash-linear-attention's fused
+    recurrent Triton kernel (fla 0.5.1, the package the reference's fla-recurrent kernel
+    was taken from, solution/triton/kernel.py:150-203).  CUPTI device time per call
+    (every kernel a call launches), L2 flushed before every call where the state fits
+    in 2x L2.  Each competitor also runs once from the same inputs as this repository's
+    kernel and the largest output / state difference is recorded."""
+    import gdn_b200
+    from gdn_b200 import synthetic
+    from gdn_b200.timing import cupti_kernels_by_name
+
+    res = {"method": "CUPTI (torch.profiler), median per kernel summed over the kernels of "
+                     "one call; L2 flushed (256 MiB write) when the state < 2x L2",
+           "iters": iters, "rows": []}
+    try:
+        from flashinfer.gdn_decode import gated_delta_rule_decode_pretranspose as fi_decode
+        from flashinfer.gdn_decode import gated_delta_rule_mtp as fi_mtp
+        res["flashinfer"] = __import__("flashinfer").__version__
+    except Exception as e:                              # noqa: BLE001
+        fi_decode = fi_mtp = None
+        res["flashinfer"] = f"unavailable: {type(e).__name__}: {e}"[:300]
+    try:
+        from fla.ops.gated_delta_rule import fused_recurrent_gated_delta_rule as fla_rec
+        res["fla"] = __import__("fla").__version__
+    except Exception as e:                              # noqa: BLE001
+        fla_rec = None
+        res["fla"] = f"unavailable: {type(e).__name__}: {e}"[:300]
+    flush_buf = l2_flush_buffer(device)
+    l2 = l2_size_bytes()
+
+    def timed(fn, state_bytes):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize(device)
+        flushed = state_bytes < 2 * l2
+        d = cupti_kernels_by_name(fn, iters, device, flush=flush_buf.zero_ if flushed else None)
+        per_call = {n: statistics.median(v) for n, v in d.items() if len(v) >= iters}
+        total = sum(per_call.values())
+        main = max(per_call, key=per_call.get) if per_call else None
+        return {"us": round(total, 3), "kernels": {n[:90]: round(t, 3) for n, t in per_call.items()},
+                "main_kernel_us": round(per_call[main], 3) if main else None,
+                "l2": "flushed" if flushed else "inputs > 2x L2"}
+
+    def diff(a, b):
+        return round(float((a.float() - b.float()).abs().max()), 6)
+
+    def row(config, impl, fn, state_bytes, nbytes, agree=None):
+        try:
+            r = timed(fn, state_bytes)
+            r.update(config=config, impl=impl, GBps=round(nbytes / r["us"] / 1e3, 1))
+            if agree is not None:
+                r["max_diff_vs_b200"] = agree
+        except Exception as e:                          # noqa: BLE001
+            r = {"config": config, "impl": impl, "error": f"{type(e).__name__}: {e}"[:300]}
+        res["rows"].append(r)
+        log(f"[compare] {config:24s} {impl:28s} {r.get('us', r.get('error'))}")
+
+    for B in (1, 8, 64, 256):
+        base = synthetic.make_inputs(B=B, seed=500 + B, device=device)
+        cfg = f"decode fp32 B={B}"
+        nbytes = synthetic.bytes_per_call(B)
+        sb = base.state.numel() * 4
+        ours = base.clone()
+        out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
+        # reference results for agreement: one step of this repository's kernel
+        ref_state = base.state.clone()
+        ref_out = torch.empty_like(out)
+        gdn_b200.kernel_cuda_b200(base.q, base.k, base.v, ref_state, base.A_log, base.a,
+                                  base.dt_bias, base.b, base.scale, ref_out, ref_state)
+        row(cfg, "b200 (this repository)",
+            lambda: gdn_b200.kernel_cuda_b200(*ours.args(), out, ours.state), sb, nbytes)
+        if fi_decode is not None:
+            fi = base.clone()
+            fo = torch.empty_like(out)
+            try:
+                fi_decode(fi.q, fi.k, fi.v, fi.state, fi.A_log, fi.a, fi.dt_bias, fi.b,
+                          scale=fi.scale, output=fo, use_qk_l2norm=False)
+                torch.cuda.synchronize(device)
+                agree = {"out": diff(fo, ref_out), "state": diff(fi.state, ref_state)}
+            except Exception as e:                      # noqa: BLE001
+                agree = {"error": f"{type(e).__name__}: {e}"[:200]}
+            row(cfg, "flashinfer fp32 (fi-baseline)",
+                lambda: fi_decode(fi.q, fi.k, fi.v, fi.state, fi.A_log, fi.a, fi.dt_bias, fi.b,
+                                  scale=fi.scale, output=fo, use_qk_l2norm=False), sb, nbytes, agree)
+        if fla_rec is not None:
+            fl = base.clone()
+            beta = torch.sigmoid(fl.b.float())          # fla takes beta; computed once, untimed
+            try:
+                fo, fs = fla_rec(fl.q, fl.k, fl.v, g=fl.a, beta=beta, scale=fl.scale,
+                                 initial_state=fl.state, output_final_state=True,
+                                 use_gate_in_kernel=True, A_log=fl.A_log, dt_bias=fl.dt_bias,
+                                 transpose_state_layout=True)
+                torch.cuda.synchronize(device)
+                agree = {"out": diff(fo, ref_out), "state": diff(fs, ref_state)}
+            except Exception as e:                      # noqa: BLE001
+                agree = {"error": f"{type(e).__name__}: {e}"[:200]}
+            row(cfg, "fla fused_recurrent (Triton)",
+                lambda: fla_rec(fl.q, fl.k, fl.v, g=fl.a, beta=beta, scale=fl.scale,
+                                initial_state=fl.state, output_final_state=True,
+                                use_gate_in_kernel=True, A_log=fl.A_log, dt_bias=fl.dt_bias,
+                                transpose_state_layout=True), sb, nbytes, agree)
+        del base, ours, out, ref_state, ref_out
+        torch.cuda.empty_cache()
+
+    for B in (1, 64, 256):
+        base = synthetic.make_inputs(B=B, seed=600 + B, device=device)
+        base.state = base.state.to(torch.bfloat16)
+        cfg = f"decode bf16 state B={B}"
+        nbytes = synthetic.bytes_per_call(B, state_elem_bytes=2)
+        sb = base.state.numel() * 2
+        ours = base.clone()
+        out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
+        ref = base.clone()
+        ref_out = gdn_b200.decode_bf16_state(ref.q, ref.k, ref.v, ref.state, ref.A_log, ref.a,
+                                             ref.dt_bias, ref.b, ref.scale)
+        row(cfg, "b200 (this repository)",
+            lambda: gdn_b200.decode_bf16_state(ours.q, ours.k, ours.v, ours.state, ours.A_log,
+                                               ours.a, ours.dt_bias, ours.b, ours.scale, out),
+            sb, nbytes)
+        if fi_decode is not None:
+            fi = base.clone()
+            fo = torch.empty_like(out)
+            try:
+                fi_decode(fi.q, fi.k, fi.v, fi.state, fi.A_log, fi.a, fi.dt_bias, fi.b,
+                          scale=fi.scale, output=fo, use_qk_l2norm=False)
+                torch.cuda.synchronize(device)
+                agree = {"out": diff(fo, ref_out), "state": diff(fi.state, ref.state),
+                         "state_bit_identical_frac": round(float(
+                             (fi.state.view(torch.int16) == ref.state.view(torch.int16))
+                             .float().mean()), 6)}
+            except Exception as e:                      # noqa: BLE001
+                agree = {"error": f"{type(e).__name__}: {e}"[:200]}
+            row(cfg, "flashinfer bf16 state",
+                lambda: fi_decode(fi.q, fi.k, fi.v, fi.state, fi.A_log, fi.a, fi.dt_bias, fi.b,
+                                  scale=fi.scale, output=fo, use_qk_l2norm=False), sb, nbytes, agree)
+        del base, ours, out, ref
+        torch.cuda.empty_cache()
+
+    for T in (2, 4):
+        B = 64
+        base = synthetic.make_inputs(B=B, T=T, seed=700 + T, device=device)
+        cfg = f"mtp fp32 B={B} T={T}"
+        nbytes = synthetic.bytes_per_call(B, T=T, intermediates=True)
+        sb = (T + 1) * base.state.numel() * 4
+        idx = torch.arange(B, dtype=torch.int32, device=device)
+        ours = base.clone()
+        out = torch.empty((B, T, HV, DIM), dtype=torch.bfloat16, device=device)
+        inter = torch.empty((B, T, HV, DIM, DIM), dtype=torch.float32, device=device)
+        ref = base.clone()
+        ref_out, _ = gdn_b200.gated_delta_rule_mtp(
+            ref.q, ref.k, ref.v, ref.state, idx, ref.A_log, ref.a, ref.dt_bias, ref.b, ref.scale,
+            None, inter, disable_state_update=False, use_qk_l2norm=False)
+        ref_inter = inter.clone()
+        row(cfg, "b200 (this repository)",
+            lambda: gdn_b200.gated_delta_rule_mtp(
+                ours.q, ours.k, ours.v, ours.state, idx, ours.A_log, ours.a, ours.dt_bias, ours.b,
+                ours.scale, out, inter, disable_state_update=False, use_qk_l2norm=False),
+            sb, nbytes)
+        if fi_mtp is not None:
+            fi = base.clone()
+            fo = torch.empty_like(out)
+            finter = torch.empty_like(inter)
+            try:
+                fi_mtp(fi.q, fi.k, fi.v, fi.state, idx, fi.A_log, fi.a, fi.dt_bias, fi.b,
+                       scale=fi.scale, output=fo, intermediate_states_buffer=finter,
+                       disable_state_update=False, use_qk_l2norm=False)
+                torch.cuda.synchronize(device)
+                agree = {"out": diff(fo, ref_out), "state": diff(fi.state, ref.state),
+                         "intermediates": diff(finter, ref_inter)}
+            except Exception as e:                      # noqa: BLE001
+                agree = {"error": f"{type(e).__name__}: {e}"[:200]}
+            row(cfg, "flashinfer mtp fp32",
+                lambda: fi_mtp(fi.q, fi.k, fi.v, fi.state, idx, fi.A_log, fi.a, fi.dt_bias, fi.b,
+                               scale=fi.scale, output=fo, intermediate_states_buffer=finter,
+                               disable_state_update=False, use_qk_l2norm=False),
+                sb, nbytes, agree)
+        del base, ours, out, inter, ref, ref_inter
+        torch.cuda.empty_cache()
+
+    with open(path, "w") as f:
+        json.dump(res, f, indent=1)
+    return res
+
+
+def run_profile_case(args):
+    """A few launches of one fixed decode case on cuda:0, then exit: the command that
+    ncu captures.  Batch 128 holds 256 MiB of fp32 state, more than the 126 MB L2 (so
+    DRAM counters mean something) and far below the sizes that make captures slow."""
+    import gdn_b200
+    from gdn_b200 import synthetic
+
+    dev = torch.device("cuda:0")
+    B, T = args.profile_case, args.T
+    slots = 4 * B if args.pooled else B
+    inp = synthetic.make_inputs(B=B, T=T, slots=slots, seed=0, device=dev)
+    idx = synthetic.make_pool_indices(B, slots, seed=0, n_pad=1, device=dev) if args.pooled else None
+    out = torch.empty((B, T, HV, DIM), dtype=torch.bfloat16, device=dev)
+    if args.bf16_state:
+        inp.state = inp.state.to(torch.bfloat16)
+    for _ in range(args.launches):
+        if args.bf16_state:
+            gdn_b200.decode_bf16_state(inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a,
+                                       inp.dt_bias, inp.b, inp.scale, out, state_indices=idx)
+        else:
+            gdn_b200.decode_tuned(inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias,
+                                  inp.b, inp.scale, out, state_indices=idx)
+    torch.cuda.synchronize(dev)
+    print(f"profile case ok: B={B} T={T} pooled={args.pooled} bf16_state={args.bf16_state} "
+          f"launches={args.launches}")
 
 
 def main():
@@ -646,15 +996,36 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--sweep", default=None, help="also write the batch sweep JSON here")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
     ap.add_argument("--skip-b1", action="store_true", help="omit the B=1 latency leg")
+    ap.add_argument("--skip-configs", action="store_true",
+                    help="omit BASELINE's other single-GPU configurations")
+    ap.add_argument("--config-iters", type=int, default=50,
+                    help="CUPTI launches per configuration")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--clock-sampler", choices=["nvml", "smi", "none"], default="nvml",
                     help="how rank 0 samples clocks during the timed region")
     ap.add_argument("--tp-collective", choices=["peer", "nccl"], default="peer",
                     help="output exchange at N > 1: fused peer stores (default) or NCCL")
+    ap.add_argument("--profile-case", type=int, default=0, metavar="B",
+                    help="run --launches decode steps at batch B on cuda:0 and exit (for ncu)")
+    ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--T", type=int, default=1, help="tokens per step of --profile-case")
+    ap.add_argument("--pooled", action="store_true",
+                    help="--profile-case: pool of 4*B slots, one -1 index")
+    ap.add_argument("--bf16-state", action="store_true", help="--profile-case: bf16 state")
+    ap.add_argument("--compare", default=None, metavar="PATH",
+                    help="time FlashInfer's and fla's decode kernels beside this one on cuda:0, "
+                         "write the table as JSON to PATH and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        run_profile_case(args)
+        return
+    if args.compare:
+        dev = torch.device("cuda:0")
+        torch.cuda.set_device(dev)
+        run_compare(dev, args.config_iters, args.compare)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank, world, local_rank = dist_env()

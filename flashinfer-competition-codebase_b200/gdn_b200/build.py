@@ -24,6 +24,10 @@ LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200.so")
 
 SOURCES = ["gdn_decode.cu"]
 TVM_LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200_tvm.so")
+# measurement-only kernels of the benchmark (the state round-trip floor), kept out of
+# the decode library
+PROBE_LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200_probe.so")
+PROBE_SOURCES = ["roofline_probe.cu"]
 TVM_SOURCES = ["tvm_ffi_entry.cu", "gdn_decode.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -116,7 +120,27 @@ def build_tvm_ffi(force: bool = False) -> str | None:
     return TVM_LIB_PATH
 
 
+def build_probe(force: bool = False) -> str:
+    """Compile libgdn_b200_probe.so (benchmark-only kernels) if missing or stale."""
+    srcs = [os.path.join(SRC_DIR, s) for s in PROBE_SOURCES]
+    deps = srcs + [os.path.abspath(__file__)]
+    if (not force and os.path.exists(PROBE_LIB_PATH)
+            and all(os.path.getmtime(d) <= os.path.getmtime(PROBE_LIB_PATH) for d in deps)):
+        return PROBE_LIB_PATH
+    os.makedirs(LIB_DIR, exist_ok=True)
+    tmp = PROBE_LIB_PATH + ".tmp"
+    cmd = [_nvcc(), *NVCC_FLAGS, "-o", tmp, *srcs]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(
+            "nvcc failed (%d):\n%s\n%s" % (proc.returncode, " ".join(cmd), proc.stderr[-8000:])
+        )
+    os.replace(tmp, PROBE_LIB_PATH)
+    return PROBE_LIB_PATH
+
+
 if __name__ == "__main__":
     force = "--force" in sys.argv
     print(build(force=force, verbose="-v" in sys.argv))
     print(build_tvm_ffi(force=force))
+    print(build_probe(force=force))

@@ -10,7 +10,7 @@ larger than the 126 MB L2 is zeroed before every launch.
 
 from __future__ import annotations
 
-from typing import Callable, List, Optional
+from typing import Callable, Dict, List, Optional
 
 import torch
 
@@ -38,4 +38,34 @@ def cupti_kernel_durations_us(fn: Callable[[], object], iters: int, device,
     for e in prof.profiler.kineto_results.events():
         if name in e.name() and str(e.device_type()).endswith("CUDA"):
             out.append(e.duration_ns() / 1e3)
+    return out
+
+
+def cupti_kernels_by_name(fn: Callable[[], object], iters: int, device,
+                          flush: Optional[Callable[[], object]] = None) -> Dict[str, List[float]]:
+    """Device durations (µs) of every kernel launched by ``iters`` calls of ``fn``,
+    grouped by kernel name; kernels that ``flush`` launches (it runs before every
+    call, inside the profiled region) are left out by name."""
+    from torch.profiler import ProfilerActivity, profile
+
+    flush_names = set()
+    if flush is not None:
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            flush()
+            torch.cuda.synchronize(device)
+        flush_names = {e.name() for e in prof.profiler.kineto_results.events()
+                       if str(e.device_type()).endswith("CUDA")}
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(iters):
+            if flush is not None:
+                flush()
+            fn()
+        torch.cuda.synchronize(device)
+    out: Dict[str, List[float]] = {}
+    for e in prof.profiler.kineto_results.events():
+        if not str(e.device_type()).endswith("CUDA") or e.name() in flush_names:
+            continue
+        if "Memcpy" in e.name() or "Memset" in e.name():
+            continue
+        out.setdefault(e.name(), []).append(e.duration_ns() / 1e3)
     return out

@@ -42,3 +42,19 @@ def test_reference_arm_other_ranks_do_nothing():
 def test_warmup_below_three_is_refused():
     res = run_bench("--steps", "2", "--warmup", "2", timeout=300)
     assert res.returncode != 0 and "warmup" in res.stderr
+
+
+def test_reference_arm_prints_the_b200_arm_config():
+    """Both arms describe the workload with the same ``config`` object."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    res = run_bench("--impl", "reference", "--steps", "2", "--warmup", "3")
+    assert res.returncode == 0, res.stderr[-2000:]
+    d = json.loads(res.stdout.strip().splitlines()[-1])
+    assert d["config"] == bench.workload_config(1, bench.l2_size_bytes())
+    for world in (1, 2, 4, 8):
+        layers, per_gpu = bench.layer_count(world, bench.B200_L2_BYTES)
+        assert layers * per_gpu >= 3 * bench.B200_L2_BYTES

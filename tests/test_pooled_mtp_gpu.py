@@ -200,9 +200,10 @@ def test_mtp_without_intermediates_t1_matches_decode():
     close_state(pool, want[1])
 
 
-def test_mtp_t4_full_heads_b64_sampled():
-    """B=64, T=4 at full head count (the benchmark shape); oracle on 4 entries."""
-    inp = synthetic.make_inputs(B=64, T=4, seed=53)
+@pytest.mark.parametrize("T", [2, 4])
+def test_mtp_full_heads_b64_sampled(T):
+    """B=64, T in {2, 4} at full head count (the benchmark shape); oracle on 4 entries."""
+    inp = synthetic.make_inputs(B=64, T=T, seed=53)
     out, pool, inter = mtp_call(inp)
     sel = torch.tensor([0, 17, 42, 63])
     sub_out, sub_pool, sub_inter = gdn_ref.decode_mtp(
@@ -212,3 +213,40 @@ def test_mtp_t4_full_heads_b64_sampled():
     close_out(out[s], sub_out)
     close_state(pool[s], sub_pool)
     close_state(inter[s], sub_inter)
+
+
+def test_baseline_pool_full_size():
+    """The benchmark's pooled configuration at full size: a 1024-slot fp32 pool
+    (2 GiB, so slot offsets pass 2^31 bytes), B = 256 entries drawn as a random
+    permutation with one -1.  Eight sampled live entries match the oracle, every
+    slot no entry reads stays bit-identical, and the -1 entry's output is zero."""
+    P, B = 1024, 256
+    inp = synthetic.make_inputs(B=B, slots=P, seed=77, device=DEV)
+    idx = synthetic.make_pool_indices(B, P, seed=77, n_pad=1, device=DEV)
+    idx_l = idx.cpu().long()
+    live = [i for i in range(B) if idx_l[i] >= 0]
+    pad = [i for i in range(B) if idx_l[i] < 0]
+    assert len(pad) == 1 and len(live) == B - 1 and max(idx_l.tolist()) >= 1000
+    sample = torch.tensor([live[j] for j in (0, 31, 64, 100, 128, 170, 222, len(live) - 1)])
+    sel = sample.to(DEV)
+    want_out, want_states = gdn_ref.decode(
+        inp.q[sel].cpu(), inp.k[sel].cpu(), inp.v[sel].cpu(), inp.state[idx[sel].long()].cpu(),
+        inp.A_log.cpu(), inp.a[sel].cpu(), inp.dt_bias.cpu(), inp.b[sel].cpu(), inp.scale)
+    before = inp.state.clone()
+    out = torch.full((B, 1, 32, 128), float("nan"), dtype=torch.bfloat16, device=DEV)
+    bad = torch.zeros(1, dtype=torch.int32, device=DEV)
+    gdn_b200.gated_delta_rule_decode_pretranspose(
+        inp.q, inp.k, inp.v, None, inp.A_log, inp.a, inp.dt_bias, inp.b, scale=inp.scale,
+        output=out, use_qk_l2norm=False, initial_state=inp.state, initial_state_indices=idx,
+        bad_index_count=bad)
+    torch.cuda.synchronize()
+    close_out(out[sel], want_out)
+    close_state(inp.state[idx[sel].long()], want_states)
+    touched = torch.zeros(P, dtype=torch.bool, device=DEV)
+    touched[idx[idx >= 0].long()] = True
+    untouched = (~touched).nonzero().flatten()
+    assert untouched.numel() == P - (B - 1)
+    for chunk in untouched.split(128):
+        assert torch.equal(inp.state[chunk], before[chunk])
+    assert torch.all(out[pad[0]] == 0)
+    assert int(bad.item()) == 0

@@ -69,10 +69,14 @@ def _rank(rank, world, port, results, collective="peer", steps=2):
         results[rank] = ("error", repr(e), traceback.format_exc()[-600:])
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("collective", ["peer", "nccl"])
-def test_tp_two_ranks_match_single_gpu(collective):
-    world, steps = 2, 3
+def test_tp_ranks_match_single_gpu(world, collective):
+    """world ranks (one GPU each) split the 16/32 heads; every rank's gathered output
+    and own state shard equal the single-GPU result on the same inputs."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    steps = 3
     inp = synthetic.make_inputs(B=12, seed=90)
     g = inp.to("cuda:0")
     want = []
