@@ -75,6 +75,10 @@ PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "gdn_step_kernel_b256.txt")
 OUT_TOL = dict(atol=1e-2, rtol=1e-2)      # bf16 output (north star)
 STATE_TOL = dict(atol=1e-3, rtol=1e-3)    # fp32 state (north star)
 PARITY_ENTRIES = (0, 85, 170, 255)        # sampled batch entries checked against the oracle
+# (label, sequence lengths, q/k heads, v-heads) of the prefill configurations
+PREFILL_CASES = (("contest qk4v8, 1 x 6 tokens (reference prefill workload 0)", [6], 4, 8),
+                 ("qwen3next 16/32, 8 x 512 tokens", [512] * 8, 16, 32),
+                 ("qwen3next 16/32, 1 x 4096 tokens", [4096], 16, 32))
 
 # NVML clock-event reason bits
 _REASONS = {
@@ -714,6 +718,9 @@ def run_configs(device, iters):
         flushed = state_bytes < 2 * l2
         d = cupti_kernel_durations_us(fn, iters, device,
                                       flush=flush_buf.zero_ if flushed else None)
+        d = [x for x in d if x > 0]
+        if not d:                     # no CUPTI records (e.g. under another profiler)
+            return dict(extra, median_us=None, GBps=None, frac=None, l2=None)
         med = statistics.median(d)
         gbs = nbytes / med / 1e3
         return dict(extra, median_us=round(med, 3), GBps=round(gbs, 1),
@@ -726,7 +733,8 @@ def run_configs(device, iters):
         out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
         fn = lambda: gdn_b200.kernel_cuda_b200(*inp.args(), out, inp.state)  # noqa: E731
         r = measure(fn, synthetic.bytes_per_call(B), inp.state.numel() * 4, {"B": B})
-        r["state_updates_per_s"] = round(B * HV / (r["median_us"] * 1e-6))
+        if r["median_us"]:
+            r["state_updates_per_s"] = round(B * HV / (r["median_us"] * 1e-6))
         res["decode_batch_sweep"].append(r)
         del inp, out
     # the same step with the in-kernel q/k L2-norm (FlashInfer's use_qk_l2norm=True;
@@ -761,6 +769,25 @@ def run_configs(device, iters):
         res["bf16_state"].append(measure(fn, synthetic.bytes_per_call(B, state_elem_bytes=2),
                                          inp.state.numel() * 2, {"B": B}))
         del inp, out
+    # variable-length prefill: the reference's prefill workload 0 shape (one 6-token
+    # sequence, 4 q/k and 8 v-heads), a batch of prompts and one long prompt at the
+    # Qwen3-Next heads (unit-norm q/k)
+    res["prefill"] = []
+    for label, lengths, H_, HV_ in PREFILL_CASES:
+        d = synthetic.make_prefill_inputs(lengths, H=H_, HV=HV_, seed=11, device=device)
+        total, N = sum(lengths), len(lengths)
+        out = torch.empty((total, HV_, DIM), dtype=torch.bfloat16, device=device)
+        ns = torch.empty((N, HV_, DIM, DIM), dtype=torch.float32, device=device)
+        fn = lambda: gdn_b200.kernel_prefill_b200(  # noqa: E731
+            d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"],
+            d["cu_seqlens"], d["scale"], out, ns)
+        r = measure(fn, synthetic.prefill_bytes(lengths, H_, HV_), 2 * ns.numel() * 4,
+                    {"case": label, "num_seqs": N, "tokens": total})
+        if r["median_us"]:
+            r["tokens_per_s"] = round(total / (r["median_us"] * 1e-6))
+            r["ns_per_token_of_longest_sequence"] = round(r["median_us"] * 1e3 / max(lengths), 2)
+        res["prefill"].append(r)
+        del d, out, ns
     # multi-token speculative verify, B = 64, one intermediate state per token
     for T in (2, 4):
         B = 64
@@ -818,9 +845,20 @@ def run_compare(device, iters, path):
         per_call = {n: statistics.median(v) for n, v in d.items() if len(v) >= iters}
         total = sum(per_call.values())
         main = max(per_call, key=per_call.get) if per_call else None
-        return {"us": round(total, 3), "kernels": {n[:90]: round(t, 3) for n, t in per_call.items()},
-                "main_kernel_us": round(per_call[main], 3) if main else None,
-                "l2": "flushed" if flushed else "inputs > 2x L2"}
+        r = {"us": round(total, 3), "kernels": {n[:90]: round(t, 3) for n, t in per_call.items()},
+             "main_kernel_us": round(per_call[main], 3) if main else None,
+             "l2": "flushed" if flushed else "inputs > 2x L2",
+             "cupti_events": {n[:60]: len(v) for n, v in d.items()}}
+        if not per_call:
+            # no kernel seen once per call: fall back to CUDA events around back-to-back calls
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize(device)
+            r.update(us=round(e0.elapsed_time(e1) * 1e3 / iters, 3), method="cuda events")
+        return r
 
     def diff(a, b):
         return round(float((a.float() - b.float()).abs().max()), 6)
@@ -956,6 +994,57 @@ def run_compare(device, iters, path):
                                disable_state_update=False, use_qk_l2norm=False),
                 sb, nbytes, agree)
         del base, ours, out, inter, ref, ref_inter
+        torch.cuda.empty_cache()
+
+    # variable-length prefill: this repository's sequential kernel against fla's chunked
+    # (WY) Triton prefill, the package the reference's prefill-fla-chunk code came from
+    # (solution/triton/fla_prefill_code.py); the same gates, q/k expanded to the v-heads
+    # and the state transposed to fla's [K, V] layout outside the timed call.
+    try:
+        from fla.ops.gated_delta_rule import chunk_gated_delta_rule as fla_chunk
+    except Exception:                                   # noqa: BLE001
+        fla_chunk = None
+    if int((torch.version.cuda or "0").split(".")[0]) < 13:
+        res["flashinfer_prefill"] = ("not run: FlashInfer's Blackwell prefill needs a CUDA 13 "
+                                     "torch (this image's is " + str(torch.version.cuda) +
+                                     "); its other path is an sm_90a kernel")
+    import torch.nn.functional as F
+    for label, lengths, H_, HV_ in PREFILL_CASES:
+        d = synthetic.make_prefill_inputs(lengths, H=H_, HV=HV_, seed=12, device=device)
+        total, N = sum(lengths), len(lengths)
+        cfg = f"prefill {label}"
+        nbytes = synthetic.prefill_bytes(lengths, H_, HV_)
+        sb = 2 * N * HV_ * DIM * DIM * 4
+        out = torch.empty((total, HV_, DIM), dtype=torch.bfloat16, device=device)
+        ns = torch.empty((N, HV_, DIM, DIM), dtype=torch.float32, device=device)
+        gdn_b200.kernel_prefill_b200(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"],
+                                     d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"], out, ns)
+        ref_out, ref_ns = out.clone(), ns.clone()
+        row(cfg, "b200 (this repository)",
+            lambda: gdn_b200.kernel_prefill_b200(
+                d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"],
+                d["cu_seqlens"], d["scale"], out, ns), sb, nbytes)
+        if fla_chunk is not None:
+            rep = HV_ // H_
+            qe = d["q"].repeat_interleave(rep, dim=1)[None]
+            ke = d["k"].repeat_interleave(rep, dim=1)[None]
+            ve = d["v"][None]
+            g = (-torch.exp(d["A_log"]) * F.softplus(d["a"].float() + d["dt_bias"]))[None]
+            beta = torch.sigmoid(d["b"].float())[None]
+            h0 = d["state"].transpose(-1, -2).contiguous()
+            cu64 = d["cu_seqlens"].long()
+            call = lambda: fla_chunk(qe, ke, ve, g, beta, scale=d["scale"],  # noqa: E731
+                                     initial_state=h0, output_final_state=True,
+                                     cu_seqlens=cu64)
+            try:
+                fo, fs = call()
+                torch.cuda.synchronize(device)
+                agree = {"out": diff(fo[0], ref_out),
+                         "state": diff(fs.transpose(-1, -2), ref_ns)}
+            except Exception as e:                      # noqa: BLE001
+                agree = {"error": f"{type(e).__name__}: {e}"[:200]}
+            row(cfg, "fla chunk_gated_delta_rule (Triton)", call, sb, nbytes, agree)
+        del d, out, ns, ref_out, ref_ns
         torch.cuda.empty_cache()
 
     with open(path, "w") as f:

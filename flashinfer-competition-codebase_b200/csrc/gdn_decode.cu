@@ -57,6 +57,8 @@ struct StepArgs {
   const int32_t* idx_in;    // [B] read slots, or null (slot = batch entry)
   const int32_t* idx_out;   // [B] write slots, or null (= read slot)
   int32_t* bad_count;       // device counter of out-of-range indices, or null
+  const int32_t* cu;        // VARLEN: [B + 1] token offsets of the B sequences
+  int total;                // VARLEN: tokens in q/k/v/a/b/out (sequence bounds clamp to it)
   float scale;
   int B, T, H, HV;
   int pool;                 // number of slots in state_in/state_out
@@ -277,8 +279,10 @@ struct TokenRaw {
 //   SCATTER (T = 1, no pool): tensor-parallel step; the CTA's output rows are
 //   staged in shared memory and stored into every rank's output buffer over
 //   NVLink, then the ranks meet at a bounded barrier (see the epilogue).
+//   VARLEN (TT == 0, no pool): variable-length prefill; batch entry bi is sequence bi
+//   with tokens cu[bi] .. cu[bi+1]-1 of flat [total, ...] inputs and state slot bi.
 template <int LPR, int RG, int W, int TT, bool POOL, bool L2N, bool SCATTER,
-          typename StateT = float>
+          typename StateT = float, bool VARLEN = false>
 __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   using Chunk = StateChunk<StateT>;
   constexpr int kVec = Chunk::kVec;     // state elements per 16-byte chunk
@@ -292,6 +296,7 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   static_assert(kDim % kRPC == 0, "rows per CTA must divide V");
   static_assert(!SCATTER || (TT == 1 && !POOL && kRPC % 8 == 0),
                 "the scatter epilogue moves whole 16-byte chunks of T=1 outputs");
+  static_assert(!VARLEN || (TT == 0 && !POOL && !SCATTER), "varlen prefill is multi-token");
   __shared__ __align__(16) uint16_t s_out[SCATTER ? kRPC : 1];
 
   const int lane = threadIdx.x & 31;
@@ -305,7 +310,14 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   const int bi = div_fast(bh, p.hv_mul, p.hv_shift);
   const int hv = bh - bi * p.HV;
   const int hq = div_fast(hv, p.hq_mul, p.hq_shift);
-  const int T = TT ? TT : p.T;
+  int T = TT ? TT : p.T;
+  int tok0 = 0;  // VARLEN: first token of the sequence
+  if constexpr (VARLEN) {
+    // sequence bounds clamped to [0, total] so that no offsets can leave the inputs
+    const int c0 = __ldg(p.cu + bi), c1 = __ldg(p.cu + bi + 1);
+    tok0 = min(max(c0, 0), p.total);
+    T = min(max(c1, tok0), p.total) - tok0;
+  }
 
   // ---- slots -------------------------------------------------------------
   int slot_in = bi;
@@ -335,7 +347,14 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   // Lane gl holds chunks gl, gl+LPR, ... of each of its rows: element
   // (c*LPR + gl)*kVec + e of the row is h[r][c*kVec + e].
   float h[RG][kEPL];
-  if (active) {
+  if (VARLEN && (p.state_in == nullptr || T == 0)) {
+    // no initial state: start from zeros; an empty sequence ends with a zero state
+    // (the reference's zero-initialised new_state, prefill_kernel.py:145-157)
+#pragma unroll
+    for (int r = 0; r < RG; ++r)
+#pragma unroll
+      for (int e = 0; e < kEPL; ++e) h[r][e] = 0.0f;
+  } else if (active) {
     const StateT* src = static_cast<const StateT*>(p.state_in) +
                         (static_cast<size_t>(slot_in) * p.HV + hv) * kHeadElems +
                         static_cast<size_t>(row0) * kDim + gl * kVec;
@@ -348,7 +367,7 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
 
   // Offsets into q/k/v/a/b/output fit in 31 bits (checked on the host).
   auto load_token = [&](int t, TokenRaw<kNC, RG, kVec>& raw) {
-    const int bt = bi * T + t;
+    const int bt = VARLEN ? tok0 + t : bi * T + t;
     const uint16_t* qp = p.q + (bt * p.H + hq) * kDim + gl * kVec;
     const uint16_t* kp = p.k + (bt * p.H + hq) * kDim + gl * kVec;
 #pragma unroll
@@ -364,7 +383,7 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   };
 
   TokenRaw<kNC, RG, kVec> cur;
-  load_token(0, cur);
+  if (!VARLEN || T > 0) load_token(0, cur);
   const float neg_exp_A = neg_exp(__ldg(p.A_log + hv));
   const float dt_b = __ldg(p.dt_bias + hv);
 
@@ -413,7 +432,7 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
       qk = group_sum<LPR>(qk);
     }
 
-    const int bt = bi * T + t;
+    const int bt = VARLEN ? tok0 + t : bi * T + t;
     uint16_t* op = p.out + (bt * p.HV + hv) * kDim + row0;
     if (active) {
 #pragma unroll
@@ -613,6 +632,38 @@ template <int TT>
 LaunchFn pick_bf16_variant(LaunchShape s, bool pool, bool l2n) {
   if (pool) return l2n ? pick_bf16_shape<TT, true, true>(s) : pick_bf16_shape<TT, true, false>(s);
   return l2n ? pick_bf16_shape<TT, false, true>(s) : pick_bf16_shape<TT, false, false>(s);
+}
+
+// Variable-length prefill kernels (fp32 state): a few work splits, with and without
+// the q/k L2-norm.
+template <int LPR, int RG, int W, bool L2N>
+cudaError_t launch_prefill(const StepArgs& p, cudaStream_t stream) {
+  constexpr int kRPC = (32 / LPR) * RG * W;
+  const long long ctas = static_cast<long long>(p.B) * p.HV * (kDim / kRPC);
+  gdn_step_kernel<LPR, RG, W, 0, false, L2N, false, float, true>
+      <<<static_cast<unsigned>(ctas), W * 32, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+LaunchFn pick_prefill(LaunchShape s, bool l2n) {
+#define GDN_PF_SHAPE(L, R, W) \
+  if (s.lpr == L && s.rg == R && s.warps == W) \
+    return l2n ? &launch_prefill<L, R, W, true> : &launch_prefill<L, R, W, false>;
+  GDN_PF_SHAPE(8, 1, 1)
+  GDN_PF_SHAPE(8, 2, 1)
+  GDN_PF_SHAPE(8, 4, 1)
+  GDN_PF_SHAPE(8, 1, 4)
+  GDN_PF_SHAPE(16, 1, 1)
+#undef GDN_PF_SHAPE
+  return nullptr;
+}
+
+// Prefill work split: the token loop of every sequence is one dependent chain per row,
+// so a few (sequence, head) pairs are spread over as many SMs as possible (4 rows per
+// CTA); many pairs keep several independent rows per lane instead.
+LaunchShape prefill_shape(long long heads) {
+  if (heads <= 64) return LaunchShape{8, 1, 1};
+  return LaunchShape{8, 4, 1};
 }
 
 // Launch shape by regime, from CUPTI sweeps of all 36 shapes on B200 (16/32 heads):
@@ -966,6 +1017,49 @@ int gdn_decode_tp_static(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v
   return gdn_decode_tp(q, k, v, state, A_log, a, dt_bias, b, scale, peer_outputs, peer_signals,
                        epochs + channel, status, timeout_us, rank, world, B, H, HV, K, V,
                        use_qk_l2norm, stream);
+}
+
+int gdn_prefill_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const float* state,
+                      const float* A_log, const gdn_bf16* a, const float* dt_bias,
+                      const gdn_bf16* b, const int32_t* cu_seqlens, double scale,
+                      gdn_bf16* output, float* new_state, int num_seqs, int total_tokens, int H,
+                      int HV, int K, int V, int use_qk_l2norm, int lanes_per_row,
+                      int rows_per_lane, int warps_per_cta, void* stream) {
+  if (K != kDim || V != kDim) return GDN_ERR_SHAPE;
+  if (num_seqs < 0 || total_tokens < 0 || H < 1 || HV < 1 || HV % H != 0) return GDN_ERR_SHAPE;
+  if (static_cast<long long>(num_seqs) * HV * kDim > 0x7fffffffLL) return GDN_ERR_SHAPE;
+  if (static_cast<long long>(total_tokens) * H > 0x7fffffffLL / kDim) return GDN_ERR_SHAPE;
+  if (static_cast<long long>(total_tokens) * HV > 0x7fffffffLL / kDim) return GDN_ERR_SHAPE;
+  if (num_seqs == 0) return GDN_OK;
+  if (!cu_seqlens || !new_state || !A_log || !dt_bias) return GDN_ERR_NULL;
+  if (total_tokens > 0 && (!q || !k || !v || !a || !b || !output)) return GDN_ERR_NULL;
+  if (!aligned(new_state, 16) || !aligned(state, 16) || !aligned(q, 8) || !aligned(k, 8) ||
+      !aligned(v, 2) || !aligned(a, 2) || !aligned(b, 2) || !aligned(output, 2) ||
+      !aligned(A_log, 4) || !aligned(dt_bias, 4) || !aligned(cu_seqlens, 4))
+    return GDN_ERR_ALIGN;
+  const size_t bytes = static_cast<size_t>(num_seqs) * HV * kHeadElems * sizeof(float);
+  if (state && state != new_state && overlaps(state, bytes, new_state, bytes)) return GDN_ERR_ALIAS;
+  StepArgs p = make_args(q, k, v, state, new_state, A_log, a, dt_bias, b, scale, output, num_seqs,
+                         1, H, HV, K, num_seqs, use_qk_l2norm);
+  p.cu = cu_seqlens;
+  p.total = total_tokens;
+  LaunchShape s = prefill_shape(static_cast<long long>(num_seqs) * HV);
+  if (lanes_per_row > 0) s.lpr = lanes_per_row;
+  if (rows_per_lane > 0) s.rg = rows_per_lane;
+  if (warps_per_cta > 0) s.warps = warps_per_cta;
+  LaunchFn fn = pick_prefill(s, p.l2norm != 0);
+  if (!fn) return GDN_ERR_SHAPE;
+  return fn(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+int gdn_prefill(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const float* state,
+                const float* A_log, const gdn_bf16* a, const float* dt_bias, const gdn_bf16* b,
+                const int32_t* cu_seqlens, double scale, gdn_bf16* output, float* new_state,
+                int num_seqs, int total_tokens, int H, int HV, int K, int V, int use_qk_l2norm,
+                void* stream) {
+  return gdn_prefill_tuned(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                           new_state, num_seqs, total_tokens, H, HV, K, V, use_qk_l2norm, 0, 0, 0,
+                           stream);
 }
 
 int gdn_interleave_heads(const gdn_bf16* gathered, gdn_bf16* output, int world, int rows, int HVl,

@@ -13,7 +13,10 @@ from .ops import (  # noqa: F401
     gated_delta_rule_decode_pretranspose,
     gated_delta_rule_mtp,
     gdn_decode,
+    gdn_prefill,
     interleave_heads,
+    kernel_prefill_b200,
+    prefill_tuned,
     kernel_cuda_b200,
     load_algo_functions,
 )
@@ -23,6 +26,9 @@ __all__ = [
     "load_library",
     "kernel_cuda_b200",
     "gdn_decode",
+    "gdn_prefill",
+    "kernel_prefill_b200",
+    "prefill_tuned",
     "gated_delta_rule_decode_pretranspose",
     "gated_delta_rule_mtp",
     "decode_bf16_state",

@@ -52,6 +52,15 @@ SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _U,
          _I, _I, _I, _I, _I, _I, _I, _I, _I, _P],
     ),
+    "gdn_prefill": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
+    ),
+    "gdn_prefill_tuned": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _I, _I, _I, _I, _I, _I, _I,
+         _I, _I, _I, _P],
+    ),
     "gdn_interleave_heads": (_I, [_P, _P, _I, _I, _I, _I, _P]),
 }
 

@@ -19,6 +19,9 @@ Entry points and the reference interfaces they stand in for:
   (``initial_state`` + ``initial_state_indices`` + ``output_state_indices``).
 * ``gated_delta_rule_mtp`` — FlashInfer's multi-token decode API
   (flashinfer/gdn_decode.py:557) for speculative verification, T >= 1.
+* ``kernel_prefill_b200`` / ``gdn_prefill`` — variable-length prefill, the
+  reference's DPS prefill entries (solution/triton/prefill_kernel.py:11-83) and the
+  value form of ``kernel_prefill_reference`` (:85-183).
 """
 
 from __future__ import annotations
@@ -363,13 +366,101 @@ def interleave_heads(gathered: torch.Tensor, output: torch.Tensor) -> torch.Tens
     return output
 
 
+def _check_prefill_inputs(q, k, v, A_log, a, dt_bias, b, cu_seqlens):
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise ValueError("q, k, v must be 3-D [total_tokens, heads, dim]")
+    total, H, K = q.shape
+    HV, V = v.shape[1], v.shape[2]
+    if K != HEAD_DIM or V != HEAD_DIM:
+        raise ValueError(f"head dims must be K == V == {HEAD_DIM}, got K={K}, V={V}")
+    if HV % H != 0:
+        raise ValueError(f"num v-heads ({HV}) must be a multiple of num q/k heads ({H})")
+    dev = q.device
+    _check(q, "q", _BF16, (total, H, K), dev)
+    _check(k, "k", _BF16, (total, H, K), dev)
+    _check(v, "v", _BF16, (total, HV, V), dev)
+    _check(A_log, "A_log", _F32, (HV,), dev)
+    _check(dt_bias, "dt_bias", _F32, (HV,), dev)
+    _check(a, "a", _BF16, (total, HV), dev)
+    _check(b, "b", _BF16, (total, HV), dev)
+    if not isinstance(cu_seqlens, torch.Tensor) or cu_seqlens.dim() != 1 or cu_seqlens.numel() < 1:
+        raise ValueError("cu_seqlens must be a 1-D tensor [num_seqs + 1]")
+    if cu_seqlens.dtype not in (torch.int32, torch.int64):
+        raise TypeError(f"cu_seqlens must be int32 or int64, got {cu_seqlens.dtype}")
+    if cu_seqlens.device != dev:
+        raise ValueError(f"cu_seqlens is on {cu_seqlens.device}, expected {dev}")
+    # int64 offsets are clamped into [0, total] before narrowing (no host sync); the
+    # kernel clamps every sequence's bounds into the same range
+    cu = cu_seqlens.clamp(0, total).to(torch.int32).contiguous()
+    return total, H, HV, K, V, cu.numel() - 1, cu, dev
+
+
+@torch.no_grad()
+def kernel_prefill_b200(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                        new_state, use_qk_l2norm: bool = False) -> None:
+    """Destination-passing variable-length prefill on the B200 kernel.
+
+    Drop-in for the reference's ``kernel_prefill_fla_chunk`` /
+    ``kernel_prefill_fi_baseline`` (solution/triton/prefill_kernel.py:11-83) with the
+    semantics of ``kernel_prefill_reference`` (:85-183): q, k [total, H, 128] bf16;
+    v [total, HV, 128] bf16; state [num_seqs, HV, 128, 128] fp32 or None (zeros);
+    a, b [total, HV] bf16; cu_seqlens [num_seqs + 1] int32/int64; output
+    [total, HV, 128] bf16 and new_state [num_seqs, HV, 128, 128] fp32 are written
+    (``new_state`` may be ``state``).  A sequence with no tokens ends with a zero state.
+    """
+    total, H, HV, K, V, N, cu, dev = _check_prefill_inputs(q, k, v, A_log, a, dt_bias, b,
+                                                            cu_seqlens)
+    if state is not None:
+        _check(state, "state", _F32, (N, HV, V, K), dev)
+    _check(new_state, "new_state", _F32, (N, HV, V, K), dev)
+    _check(output, "output", _BF16, (total, HV, V), dev)
+    with torch.cuda.device(dev):
+        _lib.call(
+            "gdn_prefill", q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(state),
+            A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), cu.data_ptr(),
+            _resolve_scale(scale, K), output.data_ptr(), new_state.data_ptr(), N, total, H, HV,
+            K, V, int(bool(use_qk_l2norm)), _stream_handle(dev))
+
+
+@torch.no_grad()
+def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None,
+                use_qk_l2norm: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Value-returning variable-length prefill, ``kernel_prefill_reference``'s form
+    (solution/triton/prefill_kernel.py:85-183): returns ``(output, new_state)``; the
+    initial ``state`` (or None for zeros) is left unchanged."""
+    total, _, HV, K, V, N, _, dev = _check_prefill_inputs(q, k, v, A_log, a, dt_bias, b,
+                                                           cu_seqlens)
+    output = torch.empty((total, HV, V), dtype=_BF16, device=dev)
+    new_state = torch.empty((N, HV, V, K), dtype=_F32, device=dev)
+    kernel_prefill_b200(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                        new_state, use_qk_l2norm=use_qk_l2norm)
+    return output, new_state
+
+
+@torch.no_grad()
+def prefill_tuned(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+                  lanes_per_row: int = 0, rows_per_lane: int = 0, warps_per_cta: int = 0) -> None:
+    """``kernel_prefill_b200`` with an explicit work split (benchmark sweeps)."""
+    total, H, HV, K, V, N, cu, dev = _check_prefill_inputs(q, k, v, A_log, a, dt_bias, b,
+                                                            cu_seqlens)
+    with torch.cuda.device(dev):
+        _lib.call(
+            "gdn_prefill_tuned", q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(state),
+            A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), cu.data_ptr(),
+            _resolve_scale(scale, K), output.data_ptr(), new_state.data_ptr(), N, total, H, HV,
+            K, V, 0, lanes_per_row, rows_per_lane, warps_per_cta, _stream_handle(dev))
+
+
 # Algorithm registry in the shape of the reference's scripts/shared.py:19-37.
 ALGO_ENTRY_POINTS = {
     "cuda-b200": "gdn_b200.ops::kernel_cuda_b200",
     "b200-value": "gdn_b200.ops::gdn_decode",
+    "prefill-b200": "gdn_b200.ops::kernel_prefill_b200",
+    "prefill-b200-value": "gdn_b200.ops::gdn_prefill",
 }
-ALGO_NO_DPS = {"b200-value"}
+ALGO_NO_DPS = {"b200-value", "prefill-b200-value"}
 
 
 def load_algo_functions() -> dict:
-    return {"cuda-b200": kernel_cuda_b200, "b200-value": gdn_decode}
+    return {"cuda-b200": kernel_cuda_b200, "b200-value": gdn_decode,
+            "prefill-b200": kernel_prefill_b200, "prefill-b200-value": gdn_prefill}

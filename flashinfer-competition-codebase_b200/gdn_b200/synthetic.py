@@ -100,3 +100,37 @@ def bytes_per_call(B: int, T: int = 1, H: int = 16, HV: int = 32, K: int = 128, 
     out = B * T * HV * V * 2
     params = 2 * HV * 4
     return traffic + qk + vv + ab + out + params
+
+
+def make_prefill_inputs(lengths, H: int = 16, HV: int = 32, seed: int = 0, device="cpu",
+                        unit_qk: bool = True, with_state: bool = True) -> dict:
+    """Token-major variable-length prefill inputs for sequences of the given lengths:
+    q, k [total, H, 128], v [total, HV, 128], a, b [total, HV], state
+    [len(lengths), HV, 128, 128] (or None), cu_seqlens int32 [len(lengths) + 1].  The
+    distributions are make_inputs'; ``unit_qk`` scales q and k to unit norm, as a
+    model's q/k producer does (long sequences of raw N(0, 1) keys make the state grow
+    by up to |1 - beta*|k|^2| per token)."""
+    total = int(sum(lengths))
+    inp = make_inputs(B=1, T=max(total, 1), H=H, HV=HV, seed=seed, slots=len(lengths),
+                      device=device)
+    q, k, v, a, b = (x[0, :total].contiguous() for x in (inp.q, inp.k, inp.v, inp.a, inp.b))
+    if unit_qk:
+        q = (q.float() / q.float().norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+        k = (k.float() / k.float().norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+    offsets = [0]
+    for n in lengths:
+        offsets.append(offsets[-1] + int(n))
+    cu = torch.tensor(offsets, dtype=torch.int32, device=device)
+    return dict(q=q, k=k, v=v, state=inp.state if with_state else None, A_log=inp.A_log, a=a,
+                dt_bias=inp.dt_bias, b=b, cu_seqlens=cu, scale=inp.scale)
+
+
+def prefill_bytes(lengths, H: int = 16, HV: int = 32, K: int = 128, V: int = 128,
+                  with_state: bool = True) -> int:
+    """Algorithmic HBM bytes of one prefill call: each sequence's state read once (when
+    given) and written once, every token's q, k, v, a, b read and output written once."""
+    total = int(sum(lengths))
+    n = len(lengths)
+    state = n * HV * V * K * 4 * (2 if with_state else 1)
+    per_token = 2 * H * K * 2 + HV * V * 2 + 2 * HV * 2 + HV * V * 2
+    return state + total * per_token + 2 * HV * 4

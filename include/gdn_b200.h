@@ -202,6 +202,48 @@ GDN_API int gdn_decode_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf1
                      int rows_per_lane, int warps_per_cta, void* stream);
 
 /*
+ * Variable-length prefill (a batch of prompts of different lengths).
+ *
+ * Replaces the reference's prefill entries for gdn_prefill_qk4_v8_d128_k_last:
+ * the destination-passing kernel_prefill_fla_chunk / kernel_prefill_fi_baseline
+ * (solution/triton/prefill_kernel.py:11-54, :57-83) with the semantics of
+ * kernel_prefill_reference (:85-183).  Flat token-major inputs:
+ *   q, k [total_tokens, H, K], v [total_tokens, HV, V], a, b [total_tokens, HV]
+ *   cu_seqlens [num_seqs + 1] int32: sequence s owns tokens cu[s] .. cu[s+1]-1
+ *   state [num_seqs, HV, V, K] fp32 initial states, or NULL for zeros
+ *   output [total_tokens, HV, V] bf16, new_state [num_seqs, HV, V, K] fp32
+ * Each sequence runs its tokens in order through the decode recurrence; the
+ * state stays in registers for the whole sequence (read once, written once).
+ * A sequence with no tokens gets a zero final state (the reference's
+ * zero-initialised new_state).  Sequence bounds are clamped to
+ * [0, total_tokens] on the device, so malformed offsets cannot address memory
+ * outside the inputs.  `state` and `new_state` may be the same buffer or
+ * disjoint.  scale == 0 selects 1/sqrt(K).
+ */
+GDN_API int gdn_prefill(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                        const float* state, const float* A_log, const gdn_bf16* a,
+                        const float* dt_bias, const gdn_bf16* b,
+                        const int32_t* cu_seqlens, double scale,
+                        gdn_bf16* output, float* new_state,
+                        int num_seqs, int total_tokens, int H, int HV, int K, int V,
+                        int use_qk_l2norm, void* stream);
+
+/*
+ * gdn_prefill with an explicit work split (no counterpart in the reference;
+ * used by the benchmark's sweeps): lanes_per_row / rows_per_lane / warps_per_cta
+ * among the built splits 8/1/1, 8/2/1, 8/4/1, 8/1/4, 16/1/1 (0 keeps the
+ * default field); other splits return GDN_ERR_SHAPE.
+ */
+GDN_API int gdn_prefill_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                              const float* state, const float* A_log, const gdn_bf16* a,
+                              const float* dt_bias, const gdn_bf16* b,
+                              const int32_t* cu_seqlens, double scale,
+                              gdn_bf16* output, float* new_state,
+                              int num_seqs, int total_tokens, int H, int HV, int K, int V,
+                              int use_qk_l2norm, int lanes_per_row, int rows_per_lane,
+                              int warps_per_cta, void* stream);
+
+/*
  * Tensor-parallel T=1 decode step with the output all-gather fused in.
  *
  * No counterpart in the reference (it runs on one GPU; its qk4/v8 contest shape

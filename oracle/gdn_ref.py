@@ -219,3 +219,36 @@ def decode_bf16_state(q, k, v, pool, state_indices, A_log, a, dt_bias, b, scale,
                 if w < P:
                     new_pool[w] = inter[i, T - 1].to(torch.bfloat16)
     return out, new_pool, (inter.to(torch.bfloat16) if keep_intermediates else None)
+
+
+@torch.no_grad()
+def prefill_varlen(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
+                   use_qk_l2norm: bool = False):
+    """Variable-length prefill, kernel_prefill_reference (prefill_kernel.py:85-183)
+    without its 4/8-head asserts: q, k [total, H, K], v [total, HV, V], a, b
+    [total, HV], state [num_seqs, HV, V, K] or None (zeros), cu_seqlens
+    [num_seqs + 1].  Sequence s runs its tokens cu[s]..cu[s+1]-1 in order from
+    state[s] (the decode step of kernel.py:95-114 per token, prefill_kernel.py:162-181).
+    A sequence with no tokens gets a zero final state, as the reference's
+    zero-initialised new_state (prefill_kernel.py:145-147, :156-157) leaves it.
+    Returns (output [total, HV, V] bf16, new_state [num_seqs, HV, V, K] fp32)."""
+    total, H, K = q.shape
+    HV, V = v.shape[1], v.shape[2]
+    scale = resolve_scale(scale, K)
+    cu = [int(x) for x in cu_seqlens.tolist()]
+    N = len(cu) - 1
+    g, beta = gates(A_log, a, dt_bias, b)                      # [total, HV]
+    output = torch.zeros(total, HV, V, dtype=torch.bfloat16)
+    new_state = torch.zeros(N, HV, V, K)
+    for s in range(N):
+        t0, t1 = cu[s], cu[s + 1]
+        if t1 <= t0:
+            continue
+        S = (state[s].float().clone() if state is not None else torch.zeros(HV, V, K))[None]
+        for t in range(t0, t1):
+            qf = _expand_qk(q[t:t + 1], HV, use_qk_l2norm)
+            kf = _expand_qk(k[t:t + 1], HV, use_qk_l2norm)
+            o, S = _step_batched(qf, kf, v[t:t + 1].float(), g[t:t + 1], beta[t:t + 1], S, scale)
+            output[t] = o[0].to(torch.bfloat16)
+        new_state[s] = S[0]
+    return output, new_state

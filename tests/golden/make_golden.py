@@ -51,6 +51,13 @@ EDGE_EDITS = {
 
 
 def apply_edits(inp, edits):
+    if edits.get("l2norm_qk"):
+        # unit-norm q and k (in fp32, rounded back to bf16), as a model's q/k producer
+        # makes them: keeps multi-token states bounded, so the comparison measures the
+        # algorithm rather than fp32 rounding amplified by |1 - beta*|k|^2| per token
+        for name in ("q", "k"):
+            x = getattr(inp, name).float()
+            setattr(inp, name, (x / x.norm(dim=-1, keepdim=True)).to(torch.bfloat16))
     for name in ("a", "b", "A_log"):
         t = getattr(inp, name)
         for pos, val in edits.get(name, []):
@@ -203,6 +210,27 @@ def main():
                                flat(inp.a), inp.dt_bias, flat(inp.b), cu, inp.scale)
         save("mtp_prefill_qk4v8_b2_t4", dict(meta, sha256=input_digest(inp)),
              output=bf16_bits(o_p.reshape(B, T, *o_p.shape[1:])), new_state=s_p.numpy())
+
+    # 7. Variable-length prefill through the reference's varlen loop on ragged
+    #    sequences: lengths 6, 0, 7, 7 (cu_seqlens [0, 6, 6, 13, 20]) — an empty
+    #    sequence among them — from a given initial state, and the same tokens from
+    #    no initial state (the reference's state=None, zeros).  q and k are unit-norm.
+    for name, with_state in (("prefill_qk4v8_ragged", True),
+                             ("prefill_qk4v8_ragged_nostate", False)):
+        if not want(name):
+            continue
+        cu_list = [0, 6, 6, 13, 20]
+        edits = {"l2norm_qk": True}
+        meta = dict(B=1, T=cu_list[-1], H=4, HV=8, seed=5, num_seqs=len(cu_list) - 1,
+                    cu_seqlens=cu_list, initial_state=with_state, edits=edits)
+        inp = apply_edits(make_inputs(B=1, T=cu_list[-1], H=4, HV=8, seed=5,
+                                      slots=len(cu_list) - 1), edits)
+        cu = torch.tensor(cu_list, dtype=torch.int32)
+        o_p, s_p = prefill_ref(inp.q[0], inp.k[0], inp.v[0], inp.state if with_state else None,
+                               inp.A_log, inp.a[0], inp.dt_bias, inp.b[0], cu, inp.scale)
+        save(name, dict(meta, sha256=input_digest(inp)), output=bf16_bits(o_p),
+             new_state=s_p.numpy())
+
 
 if __name__ == "__main__":
     main()

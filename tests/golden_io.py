@@ -21,7 +21,8 @@ from make_golden import apply_edits, input_digest  # noqa: E402
 from gdn_b200.synthetic import make_inputs, make_pool_indices  # noqa: E402
 
 NAMES = ["decode_qk4v8_b1", "decode_qk4v8_b2_edge", "decode_h16hv32_b1", "mtp_qk4v8_b1_t3",
-         "pooled_qk4v8_p5_b3", "mtp_prefill_qk4v8_b2_t4"]
+         "pooled_qk4v8_p5_b3", "mtp_prefill_qk4v8_b2_t4", "prefill_qk4v8_ragged",
+         "prefill_qk4v8_ragged_nostate"]
 
 
 def bf16_from_bits(a: np.ndarray) -> torch.Tensor:
@@ -33,7 +34,7 @@ def load(name: str):
     z = np.load(os.path.join(GOLDEN, name + ".npz"))
     meta = ast.literal_eval(str(z["meta"]))
     inp = make_inputs(B=meta["B"], T=meta["T"], H=meta["H"], HV=meta["HV"], seed=meta["seed"],
-                      slots=meta.get("slots"))
+                      slots=meta.get("slots", meta.get("num_seqs")))
     if "edits" in meta:
         inp = apply_edits(inp, meta["edits"])
     digest = input_digest(inp)

@@ -178,3 +178,28 @@ def test_tp_rejects(gdn_lib):
     assert call(outs=(ctypes.c_void_p * 2)(None, O)) == _lib.GDN_ERR_NULL
     assert call(outs=(ctypes.c_void_p * 2)(P + 4096, O)) == _lib.GDN_ERR_ALIAS
     assert call(outs=(ctypes.c_void_p * 2)(O, P + 4096), rank=1) == _lib.GDN_ERR_ALIAS
+
+
+def test_prefill_rejects(gdn_lib):
+    f = gdn_lib.gdn_prefill
+    base = dict(q=P, k=P, v=P, state=P, A_log=P, a=P, dt_bias=P, b=P, cu=P, scale=0.0,
+                out=P, new_state=P, N=2, total=8, H=16, HV=32, K=128, V=128, l2=0, stream=None)
+
+    def call(**over):
+        d = dict(base)
+        d.update(over)
+        return f(*d.values())
+
+    assert call(K=64) == _lib.GDN_ERR_SHAPE
+    assert call(HV=24) == _lib.GDN_ERR_SHAPE
+    assert call(N=-1) == _lib.GDN_ERR_SHAPE
+    assert call(total=-1) == _lib.GDN_ERR_SHAPE
+    assert call(N=0, q=None, cu=None, new_state=None) == _lib.GDN_OK   # nothing to do
+    assert call(cu=None) == _lib.GDN_ERR_NULL
+    assert call(new_state=None) == _lib.GDN_ERR_NULL
+    assert call(q=None) == _lib.GDN_ERR_NULL
+    assert call(cu=P + 2) == _lib.GDN_ERR_ALIGN
+    assert call(new_state=P + 4) == _lib.GDN_ERR_ALIGN
+    assert call(new_state=P + 4096) == _lib.GDN_ERR_ALIAS
+    args = list(base.values())[:-1]                    # all but the stream
+    assert gdn_lib.gdn_prefill_tuned(*args, 8, 3, 1, None) == _lib.GDN_ERR_SHAPE

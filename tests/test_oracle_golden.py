@@ -112,3 +112,29 @@ def test_l2norm_equals_prenormalised_inputs():
                                  inp.v[:, 0].float(), g[:, 0], beta[:, 0], S, inp.scale)
     assert_state_close(st_n, S)
     assert_bf16_close(out_n, o.unsqueeze(1).to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("name", ["prefill_qk4v8_ragged", "prefill_qk4v8_ragged_nostate"])
+def test_prefill_varlen_matches_reference_ragged(name):
+    """Ragged sequences (lengths 6, 0, 7, 7) through the reference's varlen prefill loop
+    (prefill_kernel.py:85-183): every token's output and each sequence's final state,
+    the empty sequence's final state being zero; with and without an initial state."""
+    meta, inp, gold = golden_io.load(name)
+    cu = torch.tensor(meta["cu_seqlens"], dtype=torch.int32)
+    o, s = gdn_ref.prefill_varlen(inp.q[0], inp.k[0], inp.v[0],
+                                  inp.state if meta["initial_state"] else None, inp.A_log,
+                                  inp.a[0], inp.dt_bias, inp.b[0], cu, inp.scale)
+    assert_bf16_close(o, gold["output"])
+    torch.testing.assert_close(s, gold["new_state"], rtol=1e-4, atol=1e-4)
+    assert torch.all(s[1] == 0)
+
+
+def test_prefill_varlen_matches_reference_two_sequences():
+    meta, inp, gold = golden_io.load("mtp_prefill_qk4v8_b2_t4")
+    B, T = meta["B"], meta["T"]
+    flat = lambda x: x.reshape(B * T, *x.shape[2:])    # noqa: E731
+    cu = torch.tensor([0, T, 2 * T], dtype=torch.int32)
+    o, s = gdn_ref.prefill_varlen(flat(inp.q), flat(inp.k), flat(inp.v), inp.state, inp.A_log,
+                                  flat(inp.a), inp.dt_bias, flat(inp.b), cu, inp.scale)
+    assert_bf16_close(o.reshape(B, T, *o.shape[1:]), gold["output"])
+    torch.testing.assert_close(s, gold["new_state"], rtol=1e-4, atol=1e-4)
