@@ -769,6 +769,40 @@ def run_configs(device, iters):
         res["bf16_state"].append(measure(fn, synthetic.bytes_per_call(B, state_elem_bytes=2),
                                          inp.state.numel() * 2, {"B": B}))
         del inp, out
+    # the decode step fused with the layer's gated RMSNorm, against the same step followed
+    # by the norm as separate PyTorch kernels (every kernel of a call counted)
+    from gdn_b200.timing import cupti_kernels_by_name
+    from oracle import gdn_ref  # the unfused norm below is the oracle's PyTorch ops, on GPU
+
+    res["decode_gated_norm"] = []
+    for B in (1, 256):
+        inp = synthetic.make_inputs(B=B, seed=90 + B, device=device)
+        gen = torch.Generator(device=device).manual_seed(B)
+        z = torch.randn((B, 1, HV, DIM), generator=gen, device=device).to(torch.bfloat16)
+        w = torch.ones(DIM, device=device, dtype=torch.bfloat16)
+        out = torch.empty((B, 1, HV, DIM), dtype=torch.bfloat16, device=device)
+        fused = lambda: gdn_b200.gdn_decode_gated_norm(  # noqa: E731
+            inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b, z, w,
+            scale=inp.scale, output=out)
+
+        def unfused():
+            o, _ = gdn_b200.gated_delta_rule_decode_pretranspose(
+                inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a, inp.dt_bias, inp.b,
+                scale=inp.scale, output=out, use_qk_l2norm=True)
+            return gdn_ref.gated_rmsnorm(o, z, w, 1e-6)
+
+        r = measure(fused, synthetic.bytes_per_call(B) + 2 * B * HV * DIM * 2,
+                    inp.state.numel() * 4, {"B": B})
+        flushed = inp.state.numel() * 4 < 2 * l2
+        for _ in range(5):
+            unfused()
+        d = cupti_kernels_by_name(unfused, iters, device, flush=flush_buf.zero_ if flushed else None)
+        per_call = {n: statistics.median(v) for n, v in d.items() if len(v) >= iters}
+        r["unfused_us"] = round(sum(per_call.values()), 3) if per_call else None
+        r["unfused_kernels_per_call"] = len(per_call)
+        res["decode_gated_norm"].append(r)
+        del inp, out, z, w
+
     # variable-length prefill: the reference's prefill workload 0 shape (one 6-token
     # sequence, 4 q/k and 8 v-heads), a batch of prompts and one long prompt at the
     # Qwen3-Next heads (unit-norm q/k)
@@ -803,7 +837,38 @@ def run_configs(device, iters):
     return res
 
 
-def run_compare(device, iters, path):
+COMPARE_GROUPS = ("decode_fp32", "decode_bf16", "mtp_fp32", "prefill")
+
+
+def run_compare_isolated(iters, path):
+    """run_compare with each group in a child process of its own: CUPTI activity records
+    collected through torch.profiler went missing in one process after some library
+    kernels had been JIT-built and run, so no group's timing depends on another's."""
+    import subprocess
+
+    merged = None
+    for group in COMPARE_GROUPS:
+        part = f"{path}.{group}.json"
+        rc = subprocess.run([sys.executable, os.path.abspath(__file__), "--compare", part,
+                             "--compare-group", group, "--config-iters", str(iters)]).returncode
+        try:
+            with open(part) as f:
+                d = json.load(f)
+        except (OSError, ValueError):
+            d = {"rows": [{"config": group, "error": f"child exited {rc}, no results"}]}
+        if merged is None:
+            merged = d
+        else:
+            merged["rows"] += d["rows"]
+            for key, val in d.items():
+                merged.setdefault(key, val)
+        os.remove(part) if os.path.exists(part) else None
+    with open(path, "w") as f:
+        json.dump(merged, f, indent=1)
+    return merged
+
+
+def run_compare(device, iters, path, group=None):
     """Same-GPU head-to-head with the kernels the reference measures against, on one
     GPU with local tensors only: FlashInfer's CuTe-DSL decode (fp32 state, exactly as
     the reference's kernel_fi_baseline calls it, solution/triton/kernel.py:124-147;
@@ -850,14 +915,7 @@ def run_compare(device, iters, path):
              "l2": "flushed" if flushed else "inputs > 2x L2",
              "cupti_events": {n[:60]: len(v) for n, v in d.items()}}
         if not per_call:
-            # no kernel seen once per call: fall back to CUDA events around back-to-back calls
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(iters):
-                fn()
-            e1.record()
-            torch.cuda.synchronize(device)
-            r.update(us=round(e0.elapsed_time(e1) * 1e3 / iters, 3), method="cuda events")
+            raise RuntimeError(f"CUPTI recorded no kernel once per call: {r['cupti_events']}")
         return r
 
     def diff(a, b):
@@ -874,7 +932,7 @@ def run_compare(device, iters, path):
         res["rows"].append(r)
         log(f"[compare] {config:24s} {impl:28s} {r.get('us', r.get('error'))}")
 
-    for B in (1, 8, 64, 256):
+    for B in ((1, 8, 64, 256) if group in (None, "decode_fp32") else ()):
         base = synthetic.make_inputs(B=B, seed=500 + B, device=device)
         cfg = f"decode fp32 B={B}"
         nbytes = synthetic.bytes_per_call(B)
@@ -921,7 +979,7 @@ def run_compare(device, iters, path):
         del base, ours, out, ref_state, ref_out
         torch.cuda.empty_cache()
 
-    for B in (1, 64, 256):
+    for B in ((1, 64, 256) if group in (None, "decode_bf16") else ()):
         base = synthetic.make_inputs(B=B, seed=600 + B, device=device)
         base.state = base.state.to(torch.bfloat16)
         cfg = f"decode bf16 state B={B}"
@@ -955,7 +1013,7 @@ def run_compare(device, iters, path):
         del base, ours, out, ref
         torch.cuda.empty_cache()
 
-    for T in (2, 4):
+    for T in ((2, 4) if group in (None, "mtp_fp32") else ()):
         B = 64
         base = synthetic.make_inputs(B=B, T=T, seed=700 + T, device=device)
         cfg = f"mtp fp32 B={B} T={T}"
@@ -1009,7 +1067,7 @@ def run_compare(device, iters, path):
                                      "torch (this image's is " + str(torch.version.cuda) +
                                      "); its other path is an sm_90a kernel")
     import torch.nn.functional as F
-    for label, lengths, H_, HV_ in PREFILL_CASES:
+    for label, lengths, H_, HV_ in (PREFILL_CASES if group in (None, "prefill") else ()):
         d = synthetic.make_prefill_inputs(lengths, H=H_, HV=HV_, seed=12, device=device)
         total, N = sum(lengths), len(lengths)
         cfg = f"prefill {label}"
@@ -1106,14 +1164,19 @@ def main():
     ap.add_argument("--compare", default=None, metavar="PATH",
                     help="time FlashInfer's and fla's decode kernels beside this one on cuda:0, "
                          "write the table as JSON to PATH and exit")
+    ap.add_argument("--compare-group", choices=COMPARE_GROUPS, default=None,
+                    help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args)
         return
     if args.compare:
+        if args.compare_group is None:
+            run_compare_isolated(args.config_iters, args.compare)
+            return
         dev = torch.device("cuda:0")
         torch.cuda.set_device(dev)
-        run_compare(dev, args.config_iters, args.compare)
+        run_compare(dev, args.config_iters, args.compare, group=args.compare_group)
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -71,6 +71,15 @@ struct StepArgs {
   // [hv0, hv0 + HV) of hv_total; its outputs go to every rank's output buffer.
   uint16_t* peer_out[kMaxRanks];  // [B, hv_total, V] bf16 of each rank, mapped here
   int world, hv0, hv_total;
+  // Chained tensor-parallel step (launched as a programmatic dependent of the previous
+  // step's barrier kernel): the state loads run before griddepcontrol.wait, everything
+  // else after it.
+  int chained;
+  // Gated RMSNorm epilogue (GNORM kernels only): out = bf16(bf16(w * bf16(o * r)) *
+  // silu(z)) with r = rsqrt(mean over V of o^2 + eps), o the bf16-rounded head output.
+  const uint16_t* z;        // [B, 1, HV, V] bf16 gate
+  const uint16_t* norm_w;   // [V] bf16 norm weight
+  float eps;
 };
 
 // Arguments of the cross-rank barrier that completes a tensor-parallel step.
@@ -281,8 +290,10 @@ struct TokenRaw {
 //   NVLink, then the ranks meet at a bounded barrier (see the epilogue).
 //   VARLEN (TT == 0, no pool): variable-length prefill; batch entry bi is sequence bi
 //   with tokens cu[bi] .. cu[bi+1]-1 of flat [total, ...] inputs and state slot bi.
+//   GNORM (T = 1, no pool, the CTA holds a whole head): the head's outputs go through
+//   the decode layer's gated RMSNorm before they are stored (see the epilogue).
 template <int LPR, int RG, int W, int TT, bool POOL, bool L2N, bool SCATTER,
-          typename StateT = float, bool VARLEN = false>
+          typename StateT = float, bool VARLEN = false, bool GNORM = false>
 __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   using Chunk = StateChunk<StateT>;
   constexpr int kVec = Chunk::kVec;     // state elements per 16-byte chunk
@@ -297,7 +308,10 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   static_assert(!SCATTER || (TT == 1 && !POOL && kRPC % 8 == 0),
                 "the scatter epilogue moves whole 16-byte chunks of T=1 outputs");
   static_assert(!VARLEN || (TT == 0 && !POOL && !SCATTER), "varlen prefill is multi-token");
+  static_assert(!GNORM || (TT == 1 && !POOL && !SCATTER && !VARLEN && kRPC == kDim),
+                "the gated norm needs a whole head per CTA");
   __shared__ __align__(16) uint16_t s_out[SCATTER ? kRPC : 1];
+  __shared__ float s_norm[GNORM ? kDim + 1 : 1];
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -363,6 +377,17 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
 #pragma unroll
       for (int c = 0; c < kNC; ++c)
         Chunk::load(src + r * kGroups * kDim + c * LPR * kVec, &h[r][c * kVec]);
+  }
+
+  if constexpr (SCATTER) {
+    // A chained step may start while the previous step's barrier kernel still waits
+    // for the other ranks: only the state (last written by a kernel that completed
+    // before that barrier started) is read before this point.  The wait returns once
+    // the barrier grid has completed and its memory operations are visible, so the
+    // inputs, the outputs of other ranks and this rank's peer stores below are ordered
+    // after it (the two-buffer rule of the output buffers relies on that).  Without a
+    // programmatic launch the wait returns at once.
+    if (p.chained) asm volatile("griddepcontrol.wait;" ::: "memory");
   }
 
   // Offsets into q/k/v/a/b/output fit in 31 bits (checked on the host).
@@ -453,7 +478,9 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
 #pragma unroll
         for (int e = 0; e < kEPL; ++e) h[r][e] = fmaf(dv, kf[e], g * h[r][e]);
         if (gl == 0) {
-          if constexpr (SCATTER) {
+          if constexpr (GNORM) {
+            s_norm[warp * kRPW + r * kGroups + grp] = bf16_to_f32(f32_to_bf16(o));
+          } else if constexpr (SCATTER) {
             s_out[warp * kRPW + r * kGroups + grp] = f32_to_bf16(o);
           } else {
             op[r * kGroups] = f32_to_bf16(o);
@@ -488,6 +515,36 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
         Chunk::store(dst + r * kGroups * kDim + c * LPR * kVec, &h[r][c * kVec]);
   }
 
+  if constexpr (GNORM) {
+    // Gated RMSNorm of the head's bf16 output o[0..127] (Qwen3-Next's decode layer,
+    // transformers models/qwen3_next/modeling_qwen3_next.py:73-82):
+    //   x = o * rsqrt(mean(o^2) + eps)   (fp32), rounded to bf16
+    //   y = w * x                        (bf16 * bf16, rounded to bf16)
+    //   out = y * silu(z)                (fp32), rounded to bf16
+    __syncthreads();
+    if (warp == 0) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kDim / 32; ++j) {
+        const float x = s_norm[lane * (kDim / 32) + j];
+        ss = fmaf(x, x, ss);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) s_norm[kDim] = rsqrtf(ss * (1.0f / kDim) + p.eps);
+    }
+    __syncthreads();
+    if (threadIdx.x < kDim && active) {
+      const int row = threadIdx.x;
+      const size_t off = (static_cast<size_t>(bi) * p.HV + hv) * kDim + row;
+      const float x = bf16_to_f32(f32_to_bf16(s_norm[row] * s_norm[kDim]));
+      const float y = bf16_to_f32(f32_to_bf16(bf16_to_f32(__ldg(p.norm_w + row)) * x));
+      const float zf = bf16_to_f32(__ldg(p.z + off));
+      const float silu = zf / (1.0f + expf(-zf));
+      p.out[off] = f32_to_bf16(y * silu);
+    }
+  }
+
   if constexpr (SCATTER) {
     // The CTA's kRPC outputs (one head, rows tile_in_head*kRPC ...) go to every
     // rank's output buffer as 16-byte NVLink stores, overlapping the other CTAs'
@@ -516,6 +573,9 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
 // grid, whose completion makes that grid's peer stores visible.  Each wait is
 // bounded: past timeout_ns it records the failure in *status and gives up.
 __global__ void tp_barrier_kernel(const BarrierArgs p) {
+  // Let a chained next step (a programmatic dependent) launch now: its CTAs load their
+  // state while this kernel waits, and wait for this grid before touching anything else.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ uint32_t s_epoch;
   if (threadIdx.x == 0) s_epoch = *p.epoch + 1u;
   __syncthreads();
@@ -566,6 +626,20 @@ template <int LPR, int RG, int W, int TT, bool POOL, bool L2N, bool SCATTER = fa
 cudaError_t launch_step(const StepArgs& p, cudaStream_t stream) {
   constexpr int kRPC = (32 / LPR) * RG * W;
   const long long ctas = static_cast<long long>(p.B) * p.HV * (kDim / kRPC);
+  if (SCATTER && p.chained) {
+    // programmatic dependent launch after the previous step's barrier kernel
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+    cfg.blockDim = dim3(W * 32);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gdn_step_kernel<LPR, RG, W, TT, POOL, L2N, SCATTER>, p);
+  }
   gdn_step_kernel<LPR, RG, W, TT, POOL, L2N, SCATTER>
       <<<static_cast<unsigned>(ctas), W * 32, 0, stream>>>(p);
   return cudaGetLastError();
@@ -632,6 +706,15 @@ template <int TT>
 LaunchFn pick_bf16_variant(LaunchShape s, bool pool, bool l2n) {
   if (pool) return l2n ? pick_bf16_shape<TT, true, true>(s) : pick_bf16_shape<TT, true, false>(s);
   return l2n ? pick_bf16_shape<TT, false, true>(s) : pick_bf16_shape<TT, false, false>(s);
+}
+
+// Decode step with the gated RMSNorm epilogue: one whole head per CTA (8 lanes per
+// row, 4 rows per lane, 8 warps = 128 rows), with and without the q/k L2-norm.
+template <bool L2N>
+cudaError_t launch_gated_norm(const StepArgs& p, cudaStream_t stream) {
+  gdn_step_kernel<8, 4, 8, 1, false, L2N, false, float, false, true>
+      <<<static_cast<unsigned>(static_cast<long long>(p.B) * p.HV), 256, 0, stream>>>(p);
+  return cudaGetLastError();
 }
 
 // Variable-length prefill kernels (fp32 state): a few work splits, with and without
@@ -912,12 +995,15 @@ int gdn_decode_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, fl
   return run(p, s, T == 1 ? 1 : 0, static_cast<cudaStream_t>(stream));
 }
 
-int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float* state,
-                  const float* A_log, const gdn_bf16* a, const float* dt_bias, const gdn_bf16* b,
-                  double scale, gdn_bf16* const* peer_outputs, uint32_t* const* peer_signals,
-                  uint32_t* epoch_counter, int32_t* status, uint32_t timeout_us, int rank,
-                  int world, int B, int H, int HV, int K, int V, int use_qk_l2norm,
-                  void* stream) {
+}  // extern "C"
+
+namespace {
+
+int tp_step(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float* state,
+            const float* A_log, const gdn_bf16* a, const float* dt_bias, const gdn_bf16* b,
+            double scale, gdn_bf16* const* peer_outputs, uint32_t* const* peer_signals,
+            uint32_t* epoch_counter, int32_t* status, uint32_t timeout_us, int rank, int world,
+            int B, int H, int HV, int K, int V, int use_qk_l2norm, int chained, void* stream) {
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return GDN_ERR_ARG;
   if (static_cast<long long>(HV) * world > 0x7fffffffLL / kDim) return GDN_ERR_SHAPE;
   // this rank's own output buffer is the one its outputs (and the checks) refer to
@@ -944,6 +1030,7 @@ int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float
   p.world = world;
   p.hv0 = rank * HV;
   p.hv_total = HV * world;
+  p.chained = chained ? 1 : 0;
   bar.status = status;
   bar.epoch = epoch_counter;
   bar.timeout_ns = 1000ull * (timeout_us ? timeout_us : 1000000u);
@@ -955,6 +1042,32 @@ int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float
   if (fn(p, st) != cudaSuccess) return GDN_ERR_LAUNCH;
   tp_barrier_kernel<<<1, 32, 0, st>>>(bar);
   return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float* state,
+                  const float* A_log, const gdn_bf16* a, const float* dt_bias, const gdn_bf16* b,
+                  double scale, gdn_bf16* const* peer_outputs, uint32_t* const* peer_signals,
+                  uint32_t* epoch_counter, int32_t* status, uint32_t timeout_us, int rank,
+                  int world, int B, int H, int HV, int K, int V, int use_qk_l2norm,
+                  void* stream) {
+  return tp_step(q, k, v, state, A_log, a, dt_bias, b, scale, peer_outputs, peer_signals,
+                 epoch_counter, status, timeout_us, rank, world, B, H, HV, K, V, use_qk_l2norm,
+                 0, stream);
+}
+
+int gdn_decode_tp_chained(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float* state,
+                          const float* A_log, const gdn_bf16* a, const float* dt_bias,
+                          const gdn_bf16* b, double scale, gdn_bf16* const* peer_outputs,
+                          uint32_t* const* peer_signals, uint32_t* epoch_counter,
+                          int32_t* status, uint32_t timeout_us, int rank, int world, int B, int H,
+                          int HV, int K, int V, int use_qk_l2norm, void* stream) {
+  return tp_step(q, k, v, state, A_log, a, dt_bias, b, scale, peer_outputs, peer_signals,
+                 epoch_counter, status, timeout_us, rank, world, B, H, HV, K, V, use_qk_l2norm,
+                 1, stream);
 }
 
 }  // extern "C"
@@ -1017,6 +1130,27 @@ int gdn_decode_tp_static(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v
   return gdn_decode_tp(q, k, v, state, A_log, a, dt_bias, b, scale, peer_outputs, peer_signals,
                        epochs + channel, status, timeout_us, rank, world, B, H, HV, K, V,
                        use_qk_l2norm, stream);
+}
+
+int gdn_decode_gated_norm(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, float* state,
+                          const float* A_log, const gdn_bf16* a, const float* dt_bias,
+                          const gdn_bf16* b, double scale, const gdn_bf16* z,
+                          const gdn_bf16* norm_weight, double eps, gdn_bf16* output, int B, int H,
+                          int HV, int K, int V, int use_qk_l2norm, void* stream) {
+  const int rc = check_common(q, k, v, state, A_log, a, dt_bias, b, output, B, 1, H, HV, K, V, B);
+  if (rc == kNothingToDo) return GDN_OK;
+  if (rc != GDN_OK) return rc;
+  if (!z || !norm_weight) return GDN_ERR_NULL;
+  if (!aligned(z, 2) || !aligned(norm_weight, 2)) return GDN_ERR_ALIGN;
+  if (!(eps >= 0.0)) return GDN_ERR_ARG;
+  StepArgs p = make_args(q, k, v, state, state, A_log, a, dt_bias, b, scale, output, B, 1, H, HV,
+                         K, B, use_qk_l2norm);
+  p.z = z;
+  p.norm_w = norm_weight;
+  p.eps = static_cast<float>(eps);
+  const cudaError_t e = p.l2norm ? launch_gated_norm<true>(p, static_cast<cudaStream_t>(stream))
+                                 : launch_gated_norm<false>(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
 int gdn_prefill_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const float* state,

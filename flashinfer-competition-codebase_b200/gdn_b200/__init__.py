@@ -13,6 +13,7 @@ from .ops import (  # noqa: F401
     gated_delta_rule_decode_pretranspose,
     gated_delta_rule_mtp,
     gdn_decode,
+    gdn_decode_gated_norm,
     gdn_prefill,
     interleave_heads,
     kernel_prefill_b200,
@@ -26,6 +27,7 @@ __all__ = [
     "load_library",
     "kernel_cuda_b200",
     "gdn_decode",
+    "gdn_decode_gated_norm",
     "gdn_prefill",
     "kernel_prefill_b200",
     "prefill_tuned",

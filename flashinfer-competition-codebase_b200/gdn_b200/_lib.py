@@ -47,10 +47,19 @@ SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _P, _U,
          _I, _I, _I, _I, _I, _I, _I, _I, _P],
     ),
+    "gdn_decode_tp_chained": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _P, _U,
+         _I, _I, _I, _I, _I, _I, _I, _I, _P],
+    ),
     "gdn_decode_tp_static": (
         _I,
         [_P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _U,
          _I, _I, _I, _I, _I, _I, _I, _I, _I, _P],
+    ),
+    "gdn_decode_gated_norm": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _D, _P, _I, _I, _I, _I, _I, _I, _P],
     ),
     "gdn_prefill": (
         _I,

@@ -19,6 +19,9 @@ Entry points and the reference interfaces they stand in for:
   (``initial_state`` + ``initial_state_indices`` + ``output_state_indices``).
 * ``gated_delta_rule_mtp`` — FlashInfer's multi-token decode API
   (flashinfer/gdn_decode.py:557) for speculative verification, T >= 1.
+* ``gdn_decode_gated_norm`` — the decode step fused with the decode layer's gated
+  RMSNorm of its output (Qwen3-Next's layer, transformers
+  models/qwen3_next/modeling_qwen3_next.py:73-82, :693-697).
 * ``kernel_prefill_b200`` / ``gdn_prefill`` — variable-length prefill, the
   reference's DPS prefill entries (solution/triton/prefill_kernel.py:11-83) and the
   value form of ``kernel_prefill_reference`` (:85-183).
@@ -363,6 +366,35 @@ def interleave_heads(gathered: torch.Tensor, output: torch.Tensor) -> torch.Tens
     with torch.cuda.device(dev):
         _lib.call("gdn_interleave_heads", gathered.data_ptr(), output.data_ptr(), W, rows, hvl, V,
                   _stream_handle(dev))
+    return output
+
+
+@torch.no_grad()
+def gdn_decode_gated_norm(q, k, v, state, A_log, a, dt_bias, b, z, norm_weight, scale=None,
+                          eps: float = 1e-6, use_qk_l2norm: bool = True,
+                          output=None) -> torch.Tensor:
+    """Decode step (T=1, ``state`` [B,HV,128,128] fp32 updated in place) fused with the
+    decode layer's gated RMSNorm of its output: returns
+    ``bf16(bf16(norm_weight * bf16(o * rsqrt(mean(o^2) + eps))) * silu(z))`` per
+    (batch entry, v-head), the computation of Qwen3-Next's ``Qwen3NextRMSNormGated``
+    (transformers models/qwen3_next/modeling_qwen3_next.py:73-82) applied to the step
+    output ``o`` as the layer does before its output projection (:693-697).  z
+    [B,1,HV,128] bf16; norm_weight [128] bf16.  The model's decode layer normalises q
+    and k in the kernel, hence ``use_qk_l2norm=True`` by default.  C entry:
+    ``gdn_decode_gated_norm``."""
+    B, T, H, HV, K, V, dev = _check_step_inputs(q, k, v, A_log, a, dt_bias, b, T_expected=1)
+    _check(state, "state", _F32, (B, HV, V, K), dev)
+    _check(z, "z", _BF16, (B, 1, HV, V), dev)
+    _check(norm_weight, "norm_weight", _BF16, (V,), dev)
+    if output is None:
+        output = torch.empty((B, 1, HV, V), dtype=_BF16, device=dev)
+    _check(output, "output", _BF16, (B, 1, HV, V), dev)
+    with torch.cuda.device(dev):
+        _lib.call(
+            "gdn_decode_gated_norm", q.data_ptr(), k.data_ptr(), v.data_ptr(), state.data_ptr(),
+            A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
+            _resolve_scale(scale, K), z.data_ptr(), norm_weight.data_ptr(), float(eps),
+            output.data_ptr(), B, H, HV, K, V, int(bool(use_qk_l2norm)), _stream_handle(dev))
     return output
 
 

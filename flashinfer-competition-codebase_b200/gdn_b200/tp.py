@@ -96,7 +96,8 @@ class TPDecode:
     def __init__(self, H: int, HV: int, max_batch: int, V: int = 128,
                  group: Optional[dist.ProcessGroup] = None, device=None,
                  local_step: Optional[Callable] = None, interleave: Optional[Callable] = None,
-                 collective: Optional[str] = None, timeout_us: int = 1_000_000):
+                 collective: Optional[str] = None, timeout_us: int = 1_000_000,
+                 chain: bool = True):
         self.group = group
         world = dist.get_world_size(group)
         rank = dist.get_rank(group)
@@ -110,6 +111,9 @@ class TPDecode:
             raise ValueError(f"collective must be 'peer' or 'nccl', got {collective!r}")
         self.collective = collective
         self.timeout_us = int(timeout_us)
+        # captured sequences launch each step after the first as a programmatic
+        # dependent of the previous step's barrier (gdn_decode_tp_chained)
+        self.chain = bool(chain)
         self._steps = 0              # host count of peer steps: output buffer parity
         n = max_batch * self.shard.hv_local * V
         if collective == "nccl":
@@ -146,7 +150,8 @@ class TPDecode:
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
 
-    def _peer_step(self, q, k, v, state, A_log, a, dt_bias, b, scale, B, events, parity=None):
+    def _peer_step(self, q, k, v, state, A_log, a, dt_bias, b, scale, B, events, parity=None,
+                   chained=False):
         from . import _lib
         from .ops import _check, _check_step_inputs, _resolve_scale
 
@@ -162,7 +167,8 @@ class TPDecode:
             e0.record()
         with torch.cuda.device(dev):
             _lib.call(
-                "gdn_decode_tp", q.data_ptr(), k.data_ptr(), v.data_ptr(), state.data_ptr(),
+                "gdn_decode_tp_chained" if chained else "gdn_decode_tp",
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), state.data_ptr(),
                 A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(),
                 _resolve_scale(scale, K), self._peer_out[parity], self._peer_sig,
                 self._epoch.data_ptr(), self.status.data_ptr(), self.timeout_us,
@@ -208,7 +214,10 @@ class TPDecode:
                 for i, args in enumerate(step_args):
                     parity = (start + i) & 1
                     if self.collective == "peer":
-                        out = self._peer_step(*args, args[0].shape[0], None, parity=parity)
+                        # steps after the first follow the previous step's barrier kernel
+                        # directly: their decode kernels start loading state while it waits
+                        out = self._peer_step(*args, args[0].shape[0], None, parity=parity,
+                                              chained=self.chain and i > 0)
                     else:
                         out = self.step(*args)
             graphs.append(g)

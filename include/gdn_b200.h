@@ -202,6 +202,30 @@ GDN_API int gdn_decode_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf1
                      int rows_per_lane, int warps_per_cta, void* stream);
 
 /*
+ * Fused T=1 decode step plus the decode layer's gated RMSNorm, state in place.
+ *
+ * The decode step of gdn_decode (state [B, HV, V, K] updated in place; the
+ * reference's step, solution/triton/kernel.py:95-114) followed, inside the same
+ * kernel, by the gated RMSNorm that Qwen3-Next applies to the step's output
+ * before the output projection (the layer the reference's contest shapes come
+ * from, CLAUDE.md:67-84; transformers models/qwen3_next/modeling_qwen3_next.py:73-82
+ * and :693-697), per (batch entry, v-head) over the V = 128 outputs o (bf16):
+ *   x   = bf16(o * rsqrt(mean(o^2) + eps))
+ *   y   = bf16(norm_weight * x)
+ *   out = bf16(y * silu(z))
+ * z [B, 1, HV, V] bf16 is the layer's gate projection, norm_weight [V] bf16.
+ * `output` [B, 1, HV, V] receives the normalised values (the raw o is not
+ * stored).  One CTA holds a whole head, so the norm needs no second kernel.
+ * eps must be >= 0 (GDN_ERR_ARG otherwise).
+ */
+GDN_API int gdn_decode_gated_norm(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                                  float* state, const float* A_log, const gdn_bf16* a,
+                                  const float* dt_bias, const gdn_bf16* b, double scale,
+                                  const gdn_bf16* z, const gdn_bf16* norm_weight, double eps,
+                                  gdn_bf16* output, int B, int H, int HV, int K, int V,
+                                  int use_qk_l2norm, void* stream);
+
+/*
  * Variable-length prefill (a batch of prompts of different lengths).
  *
  * Replaces the reference's prefill entries for gdn_prefill_qk4_v8_d128_k_last:
@@ -284,6 +308,26 @@ GDN_API int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* 
                           uint32_t* epoch_counter, int32_t* status, uint32_t timeout_us,
                           int rank, int world, int B, int H, int HV, int K, int V,
                           int use_qk_l2norm, void* stream);
+
+/*
+ * gdn_decode_tp for the next step of a sequence of steps enqueued back to back on
+ * one stream (no counterpart in the reference).  The decode kernel is launched as
+ * a programmatic dependent of the previous call's barrier kernel: its CTAs load
+ * their state while that barrier still waits for the other ranks, and wait for
+ * the barrier grid (griddepcontrol.wait) before reading any other input or
+ * storing any output.  Requires that the kernel enqueued on `stream` right
+ * before this call is the barrier of a previous gdn_decode_tp /
+ * gdn_decode_tp_chained call (that barrier started only after its own decode
+ * kernel, so every state those steps wrote is complete), and that nothing that
+ * writes `state` runs between them.  Results are identical to gdn_decode_tp.
+ */
+GDN_API int gdn_decode_tp_chained(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                                  float* state, const float* A_log, const gdn_bf16* a,
+                                  const float* dt_bias, const gdn_bf16* b, double scale,
+                                  gdn_bf16* const* peer_outputs, uint32_t* const* peer_signals,
+                                  uint32_t* epoch_counter, int32_t* status, uint32_t timeout_us,
+                                  int rank, int world, int B, int H, int HV, int K, int V,
+                                  int use_qk_l2norm, void* stream);
 
 /*
  * Allocation-free variant of gdn_decode_tp.  No counterpart in the reference.

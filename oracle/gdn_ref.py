@@ -252,3 +252,18 @@ def prefill_varlen(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
             output[t] = o[0].to(torch.bfloat16)
         new_state[s] = S[0]
     return output, new_state
+
+
+@torch.no_grad()
+def gated_rmsnorm(o, z, weight, eps: float = 1e-6):
+    """The decode layer's gated RMSNorm of the step output, in the order of
+    Qwen3-Next's ``Qwen3NextRMSNormGated.forward`` (transformers
+    models/qwen3_next/modeling_qwen3_next.py:73-82): o and z bf16 [..., V], weight
+    bf16 [V]; fp32 normalisation, rounded to bf16, times the bf16 weight (a bf16
+    product), times silu(z) in fp32, rounded to bf16."""
+    x = o.float()
+    var = x.pow(2).mean(-1, keepdim=True)
+    x = x * torch.rsqrt(var + eps)
+    x = weight * x.to(torch.bfloat16)
+    x = x * F.silu(z.float())
+    return x.to(torch.bfloat16)

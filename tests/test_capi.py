@@ -203,3 +203,22 @@ def test_prefill_rejects(gdn_lib):
     assert call(new_state=P + 4096) == _lib.GDN_ERR_ALIAS
     args = list(base.values())[:-1]                    # all but the stream
     assert gdn_lib.gdn_prefill_tuned(*args, 8, 3, 1, None) == _lib.GDN_ERR_SHAPE
+
+
+def test_gated_norm_rejects(gdn_lib):
+    f = gdn_lib.gdn_decode_gated_norm
+    # valid except for the one field each call changes: every call fails validation
+    # (or is the B = 0 no-op) before anything is launched
+    args = [P] * 8 + [0.0, P, P, 1e-6, P, 1, 16, 32, 128, 128, 1, None]
+    bad_eps = list(args)
+    bad_eps[11] = -1.0
+    assert f(*bad_eps) == _lib.GDN_ERR_ARG
+    no_z = list(args)
+    no_z[9] = None
+    assert f(*no_z) == _lib.GDN_ERR_NULL
+    odd_w = list(args)
+    odd_w[10] = P + 1
+    assert f(*odd_w) == _lib.GDN_ERR_ALIGN
+    zero_b = list(args)
+    zero_b[13] = 0
+    assert f(*zero_b) == _lib.GDN_OK

@@ -105,7 +105,9 @@ def test_long_sequence_sampled_heads():
 
 
 @pytest.mark.parametrize("shape", [(8, 1, 1), (8, 2, 1), (8, 4, 1), (8, 1, 4), (16, 1, 1)])
-def test_every_built_work_split_is_bit_identical_to_the_default(shape):
+def test_every_built_work_split_matches_the_default(shape):
+    """Splits with the default 8 lanes per row reduce in the same order: bit-identical.
+    16 lanes per row add the partial sums in another order: within the tolerances."""
     d = to_dev(flat_inputs([7, 33, 1], seed=6))
     total, N = d["v"].shape[0], d["cu_seqlens"].numel() - 1
     ref_o, ref_s = gdn_b200.gdn_prefill(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"],
@@ -115,7 +117,11 @@ def test_every_built_work_split_is_bit_identical_to_the_default(shape):
     gdn_b200.prefill_tuned(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"],
                            d["b"], d["cu_seqlens"], d["scale"], out, ns, *shape)
     torch.cuda.synchronize()
-    assert torch.equal(out, ref_o) and torch.equal(ns, ref_s)
+    if shape[0] == 8:
+        assert torch.equal(out, ref_o) and torch.equal(ns, ref_s)
+    else:
+        torch.testing.assert_close(out.float(), ref_o.float(), **OUT_TOL)
+        torch.testing.assert_close(ns, ref_s, **STATE_TOL)
 
 
 def test_offsets_outside_the_tokens_are_clamped():

@@ -137,6 +137,32 @@ def test_fused_step_single_rank_matches_plain_kernel(B):
     assert int(status.item()) == 0 and int(sig[0].item()) == 3 and int(epoch.item()) == 3
 
 
+@pytest.mark.parametrize("B", [1, 64])
+def test_chained_steps_match_plain_steps(B):
+    """world = 1: one gdn_decode_tp, then gdn_decode_tp_chained steps enqueued back to
+    back (each decode kernel a programmatic dependent of the previous barrier, loading
+    the state that the previous decode wrote) give the plain kernel's results exactly."""
+    P = ctypes.c_void_p
+    inp = synthetic.make_inputs(B=B, seed=98)
+    g, h = inp.to("cuda"), inp.to("cuda")
+    outs = [torch.zeros((B, 1, 32, 128), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    sig = torch.zeros(8, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    epoch = torch.zeros(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for step in range(4):
+        _lib.call("gdn_decode_tp_chained" if step else "gdn_decode_tp",
+                  g.q.data_ptr(), g.k.data_ptr(), g.v.data_ptr(), g.state.data_ptr(),
+                  g.A_log.data_ptr(), g.a.data_ptr(), g.dt_bias.data_ptr(), g.b.data_ptr(),
+                  g.scale, (P * 1)(outs[step & 1].data_ptr()), (P * 1)(sig.data_ptr()),
+                  epoch.data_ptr(), status.data_ptr(), 0, 0, 1, B, 16, 32, 128, 128, 0, stream)
+    for _ in range(4):                     # the same steps with the plain kernel, afterwards
+        want, _ = gdn_b200.gdn_decode(*h.args())
+    torch.cuda.synchronize()
+    assert torch.equal(outs[1], want) and torch.equal(g.state, h.state)
+    assert int(status.item()) == 0 and int(epoch.item()) == 4
+
+
 def test_fused_step_replays_from_cuda_graphs():
     """world = 1 through TPDecode.capture: the barrier's epoch lives on the device,
     so replayed graphs keep advancing it; outputs alternate between two buffers."""
