@@ -907,7 +907,8 @@ def run_compare(device, iters, path, group=None):
         torch.cuda.synchronize(device)
         flushed = state_bytes < 2 * l2
         d = cupti_kernels_by_name(fn, iters, device, flush=flush_buf.zero_ if flushed else None)
-        per_call = {n: statistics.median(v) for n, v in d.items() if len(v) >= iters}
+        # kernels seen once per call (CUPTI can drop a few records of a long run)
+        per_call = {n: statistics.median(v) for n, v in d.items() if len(v) >= 0.9 * iters}
         total = sum(per_call.values())
         main = max(per_call, key=per_call.get) if per_call else None
         r = {"us": round(total, 3), "kernels": {n[:90]: round(t, 3) for n, t in per_call.items()},

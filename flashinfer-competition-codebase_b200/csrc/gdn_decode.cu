@@ -709,11 +709,17 @@ LaunchFn pick_bf16_variant(LaunchShape s, bool pool, bool l2n) {
 }
 
 // Decode step with the gated RMSNorm epilogue: one whole head per CTA (8 lanes per
-// row, 4 rows per lane, 8 warps = 128 rows), with and without the q/k L2-norm.
+// row and 4 rows per lane in 8 warps, or 1 row per lane in 32 warps = 128 rows), with
+// and without the q/k L2-norm.
+// At small batch (few heads, so few CTAs) a head gets 32 warps of 4 rows each, which keeps
+// as many state loads in flight per CTA as the plain step's default split does.
 template <bool L2N>
 cudaError_t launch_gated_norm(const StepArgs& p, cudaStream_t stream) {
-  gdn_step_kernel<8, 4, 8, 1, false, L2N, false, float, false, true>
-      <<<static_cast<unsigned>(static_cast<long long>(p.B) * p.HV), 256, 0, stream>>>(p);
+  const unsigned ctas = static_cast<unsigned>(static_cast<long long>(p.B) * p.HV);
+  if (static_cast<long long>(p.B) * p.HV <= 512)
+    gdn_step_kernel<8, 1, 32, 1, false, L2N, false, float, false, true><<<ctas, 1024, 0, stream>>>(p);
+  else
+    gdn_step_kernel<8, 4, 8, 1, false, L2N, false, float, false, true><<<ctas, 256, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
