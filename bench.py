@@ -716,7 +716,8 @@ def run_configs(device, iters):
         for _ in range(5):
             fn()
         flushed = state_bytes < 2 * l2
-        d = cupti_kernel_durations_us(fn, iters, device,
+        # every kernel of this library (gdn_step_kernel, gdn_prefill_chunk_kernel)
+        d = cupti_kernel_durations_us(fn, iters, device, name="gdn_",
                                       flush=flush_buf.zero_ if flushed else None)
         d = [x for x in d if x > 0]
         if not d:                     # no CUPTI records (e.g. under another profiler)

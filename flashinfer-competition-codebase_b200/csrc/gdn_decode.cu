@@ -1197,6 +1197,14 @@ int gdn_prefill(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const f
                 const int32_t* cu_seqlens, double scale, gdn_bf16* output, float* new_state,
                 int num_seqs, int total_tokens, int H, int HV, int K, int V, int use_qk_l2norm,
                 void* stream) {
+  // Sequences of 32 tokens or more on average go to the chunked tensor-core kernel (one
+  // chunk costs about what 15-25 dependent token updates cost in the register-resident
+  // loop); shorter ones, the q/k L2-norm option and inputs without 16-byte alignment stay
+  // on the token loop.  Both compute the same recurrence.
+  if (!use_qk_l2norm && num_seqs > 0 && total_tokens >= 32LL * num_seqs &&
+      aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(output, 16))
+    return gdn_prefill_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                               new_state, nullptr, num_seqs, total_tokens, H, HV, K, V, stream);
   return gdn_prefill_tuned(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
                            new_state, num_seqs, total_tokens, H, HV, K, V, use_qk_l2norm, 0, 0, 0,
                            stream);

@@ -17,6 +17,7 @@ from .ops import (  # noqa: F401
     gdn_prefill,
     interleave_heads,
     kernel_prefill_b200,
+    prefill_chunked,
     prefill_tuned,
     kernel_cuda_b200,
     load_algo_functions,
@@ -30,6 +31,7 @@ __all__ = [
     "gdn_decode_gated_norm",
     "gdn_prefill",
     "kernel_prefill_b200",
+    "prefill_chunked",
     "prefill_tuned",
     "gated_delta_rule_decode_pretranspose",
     "gated_delta_rule_mtp",

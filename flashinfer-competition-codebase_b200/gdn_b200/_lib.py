@@ -65,6 +65,10 @@ SIGNATURES = {
         _I,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P],
     ),
+    "gdn_prefill_chunked": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
+    ),
     "gdn_prefill_tuned": (
         _I,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _I, _I, _I, _I, _I, _I, _I,

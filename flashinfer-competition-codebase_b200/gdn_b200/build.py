@@ -22,13 +22,13 @@ INCLUDE_DIR = os.path.join(os.path.dirname(os.path.dirname(PKG_DIR)), "include")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200.so")
 
-SOURCES = ["gdn_decode.cu"]
+SOURCES = ["gdn_decode.cu", "gdn_prefill_chunked.cu"]
 TVM_LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200_tvm.so")
 # measurement-only kernels of the benchmark (the state round-trip floor), kept out of
 # the decode library
 PROBE_LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200_probe.so")
 PROBE_SOURCES = ["roofline_probe.cu"]
-TVM_SOURCES = ["tvm_ffi_entry.cu", "gdn_decode.cu"]
+TVM_SOURCES = ["tvm_ffi_entry.cu", "gdn_decode.cu", "gdn_prefill_chunked.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo",

@@ -470,6 +470,29 @@ def gdn_prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale=None,
 
 
 @torch.no_grad()
+def prefill_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+                    status=None) -> torch.Tensor:
+    """``kernel_prefill_b200`` computed by 64-token chunks on the tensor cores (C entry
+    ``gdn_prefill_chunked``).  Returns the int32 status tensor (1 if a wait for the
+    tensor cores timed out)."""
+    total, H, HV, K, V, N, cu, dev = _check_prefill_inputs(q, k, v, A_log, a, dt_bias, b,
+                                                            cu_seqlens)
+    if state is not None:
+        _check(state, "state", _F32, (N, HV, V, K), dev)
+    _check(new_state, "new_state", _F32, (N, HV, V, K), dev)
+    _check(output, "output", _BF16, (total, HV, V), dev)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call(
+            "gdn_prefill_chunked", q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(state),
+            A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), cu.data_ptr(),
+            _resolve_scale(scale, K), output.data_ptr(), new_state.data_ptr(), status.data_ptr(),
+            N, total, H, HV, K, V, _stream_handle(dev))
+    return status
+
+
+@torch.no_grad()
 def prefill_tuned(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
                   lanes_per_row: int = 0, rows_per_lane: int = 0, warps_per_cta: int = 0) -> None:
     """``kernel_prefill_b200`` with an explicit work split (benchmark sweeps)."""

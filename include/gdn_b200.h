@@ -236,8 +236,11 @@ GDN_API int gdn_decode_gated_norm(const gdn_bf16* q, const gdn_bf16* k, const gd
  *   cu_seqlens [num_seqs + 1] int32: sequence s owns tokens cu[s] .. cu[s+1]-1
  *   state [num_seqs, HV, V, K] fp32 initial states, or NULL for zeros
  *   output [total_tokens, HV, V] bf16, new_state [num_seqs, HV, V, K] fp32
- * Each sequence runs its tokens in order through the decode recurrence; the
- * state stays in registers for the whole sequence (read once, written once).
+ * Each sequence runs its tokens in order through the decode recurrence.  When
+ * the sequences average 32 tokens or more (and q, k, v, output are 16-byte
+ * aligned, use_qk_l2norm == 0) the call runs gdn_prefill_chunked, the chunked
+ * tensor-core form of the same recurrence; otherwise a token loop whose state
+ * stays in registers for the whole sequence (read once, written once).
  * A sequence with no tokens gets a zero final state (the reference's
  * zero-initialised new_state).  Sequence bounds are clamped to
  * [0, total_tokens] on the device, so malformed offsets cannot address memory
@@ -251,6 +254,29 @@ GDN_API int gdn_prefill(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
                         gdn_bf16* output, float* new_state,
                         int num_seqs, int total_tokens, int H, int HV, int K, int V,
                         int use_qk_l2norm, void* stream);
+
+/*
+ * Variable-length prefill by chunks of 64 tokens on the tensor cores (tcgen05).
+ *
+ * Same operation, arguments and results as gdn_prefill (the reference's prefill
+ * entries, solution/triton/prefill_kernel.py:11-83, with kernel_prefill_reference's
+ * semantics, :85-183), computed in the chunked (WY) form of the delta rule that the
+ * reference's own prefill path uses (solution/triton/fla_prefill_code.py): per chunk
+ * of 64 tokens a handful of matrix products (bf16 for the chunk's own q/k/v, tf32
+ * against the fp32 state, fp32 accumulation) replace 64 dependent rank-1 updates.
+ * One CTA per (sequence, v-head), state resident in tensor memory; q, k, v, the
+ * output and the states must be 16-byte aligned.  Results agree with the token loop to within the
+ * accuracy of the split-bf16 / tf32 products (about 1e-4 relative on the state),
+ * not bit for bit.  `status` (device int32, may be NULL, never cleared here) is set
+ * to 1 if a bounded wait for the tensor cores or a TMA load timed out.
+ */
+GDN_API int gdn_prefill_chunked(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                                const float* state, const float* A_log, const gdn_bf16* a,
+                                const float* dt_bias, const gdn_bf16* b,
+                                const int32_t* cu_seqlens, double scale,
+                                gdn_bf16* output, float* new_state, int32_t* status,
+                                int num_seqs, int total_tokens, int H, int HV, int K, int V,
+                                void* stream);
 
 /*
  * gdn_prefill with an explicit work split (no counterpart in the reference;

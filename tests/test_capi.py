@@ -222,3 +222,22 @@ def test_gated_norm_rejects(gdn_lib):
     zero_b = list(args)
     zero_b[13] = 0
     assert f(*zero_b) == _lib.GDN_OK
+
+
+def test_prefill_chunked_rejects(gdn_lib):
+    f = gdn_lib.gdn_prefill_chunked
+    base = dict(q=P, k=P, v=P, state=P, A_log=P, a=P, dt_bias=P, b=P, cu=P, scale=0.0,
+                out=P, new_state=P, status=None, N=2, total=8, H=16, HV=32, K=128, V=128,
+                stream=None)
+
+    def call(**over):
+        d = dict(base)
+        d.update(over)
+        return f(*d.values())
+
+    assert call(K=64) == _lib.GDN_ERR_SHAPE
+    assert call(N=0, q=None, cu=None) == _lib.GDN_OK
+    assert call(cu=None) == _lib.GDN_ERR_NULL
+    assert call(q=P + 8) == _lib.GDN_ERR_ALIGN        # TMA sources need 16-byte alignment
+    assert call(out=P + 2) == _lib.GDN_ERR_ALIGN
+    assert call(new_state=P + 4096) == _lib.GDN_ERR_ALIAS
