@@ -1112,6 +1112,26 @@ def run_compare(device, iters, path, group=None):
     return res
 
 
+def run_profile_prefill(args):
+    """A few variable-length prefill calls on cuda:0 (16/32 heads, unit-norm q/k), then
+    exit: the command that ncu captures for the prefill kernels."""
+    import gdn_b200
+    from gdn_b200 import synthetic
+
+    dev = torch.device("cuda:0")
+    lengths = [int(x) for x in args.profile_prefill.split(",")]
+    d = synthetic.make_prefill_inputs(lengths, seed=11, device=dev)
+    total, N = sum(lengths), len(lengths)
+    out = torch.empty((total, HV, DIM), dtype=torch.bfloat16, device=dev)
+    ns = torch.empty((N, HV, DIM, DIM), dtype=torch.float32, device=dev)
+    for _ in range(args.launches):
+        gdn_b200.kernel_prefill_b200(d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"],
+                                     d["dt_bias"], d["b"], d["cu_seqlens"], d["scale"], out, ns)
+    torch.cuda.synchronize(dev)
+    print(f"profile prefill ok: lengths={lengths[:4]}{'...' if N > 4 else ''} x{N} "
+          f"launches={args.launches}")
+
+
 def run_profile_case(args):
     """A few launches of one fixed decode case on cuda:0, then exit: the command that
     ncu captures.  Batch 128 holds 256 MiB of fp32 state, more than the 126 MB L2 (so
@@ -1127,8 +1147,14 @@ def run_profile_case(args):
     out = torch.empty((B, T, HV, DIM), dtype=torch.bfloat16, device=dev)
     if args.bf16_state:
         inp.state = inp.state.to(torch.bfloat16)
+    if args.gated_norm:
+        z = torch.randn((B, T, HV, DIM), device=dev).to(torch.bfloat16)
+        w = torch.ones(DIM, device=dev, dtype=torch.bfloat16)
     for _ in range(args.launches):
-        if args.bf16_state:
+        if args.gated_norm:
+            gdn_b200.gdn_decode_gated_norm(inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a,
+                                           inp.dt_bias, inp.b, z, w, scale=inp.scale, output=out)
+        elif args.bf16_state:
             gdn_b200.decode_bf16_state(inp.q, inp.k, inp.v, inp.state, inp.A_log, inp.a,
                                        inp.dt_bias, inp.b, inp.scale, out, state_indices=idx)
         else:
@@ -1136,7 +1162,7 @@ def run_profile_case(args):
                                   inp.b, inp.scale, out, state_indices=idx)
     torch.cuda.synchronize(dev)
     print(f"profile case ok: B={B} T={T} pooled={args.pooled} bf16_state={args.bf16_state} "
-          f"launches={args.launches}")
+          f"gated_norm={args.gated_norm} launches={args.launches}")
 
 
 def main():
@@ -1163,6 +1189,11 @@ def main():
     ap.add_argument("--pooled", action="store_true",
                     help="--profile-case: pool of 4*B slots, one -1 index")
     ap.add_argument("--bf16-state", action="store_true", help="--profile-case: bf16 state")
+    ap.add_argument("--gated-norm", action="store_true",
+                    help="--profile-case: the step fused with the gated RMSNorm")
+    ap.add_argument("--profile-prefill", default=None, metavar="LENGTHS",
+                    help="run --launches prefill calls with these comma-separated sequence "
+                         "lengths on cuda:0 and exit (for ncu)")
     ap.add_argument("--compare", default=None, metavar="PATH",
                     help="time FlashInfer's and fla's decode kernels beside this one on cuda:0, "
                          "write the table as JSON to PATH and exit")
@@ -1171,6 +1202,9 @@ def main():
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args)
+        return
+    if args.profile_prefill:
+        run_profile_prefill(args)
         return
     if args.compare:
         if args.compare_group is None:

@@ -50,11 +50,18 @@ def cupti_kernels_by_name(fn: Callable[[], object], iters: int, device,
 
     flush_names = set()
     if flush is not None:
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            flush()
-            torch.cuda.synchronize(device)
-        flush_names = {e.name() for e in prof.profiler.kineto_results.events()
-                       if str(e.device_type()).endswith("CUDA")}
+        # a profiling session right after a JIT compile can come back without records:
+        # try a few times, and refuse to time with the flush mixed into the results
+        for _ in range(4):
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                flush()
+                torch.cuda.synchronize(device)
+            flush_names = {e.name() for e in prof.profiler.kineto_results.events()
+                           if str(e.device_type()).endswith("CUDA")}
+            if flush_names:
+                break
+        if not flush_names:
+            raise RuntimeError("CUPTI recorded no kernel of the L2 flush")
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         for _ in range(iters):
             if flush is not None:
