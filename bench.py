@@ -64,7 +64,8 @@ for _p in (PKG_ROOT, ROOT):
 
 import torch  # noqa: E402
 
-from gdn_b200.timing import cupti_kernel_durations_us, l2_flush_buffer  # noqa: E402
+from gdn_b200.timing import (  # noqa: E402
+    cupti_kernel_durations_us, cupti_kernels_by_name, l2_flush_buffer)
 
 METRIC = "GDN decode µs (CUPTI) at B=1; state-update HBM GB/s vs peak at B=256"
 UNIT = "GB/s"
@@ -364,7 +365,7 @@ def b1_latency(device, iters=200):
 
     for _ in range(20):
         fn()
-    d = cupti_kernel_durations_us(fn, iters, device, flush=flush_buf.zero_)
+    d = cupti_kernel_durations_us(fn, iters, device, flush=flush_buf.bitwise_not_)
     d_warm = cupti_kernel_durations_us(fn, iters, device, flush=None)
     # floor of the method: this repository's own kernel that reads and writes the same
     # 2 MiB state in place with the decode kernel's grid, work split and cache hints
@@ -381,9 +382,9 @@ def b1_latency(device, iters=200):
     for _ in range(20):
         floor_fn()
     floor = cupti_kernel_durations_us(floor_fn, iters, device, name="roundtrip_kernel",
-                                      flush=flush_buf.zero_)
+                                      flush=flush_buf.bitwise_not_)
     res = {"median_us": None, "source": "cupti (torch.profiler activity records)",
-           "l2": "flushed before every launch (256 MiB write)", "iters": len(d)}
+           "l2": "flushed before every launch (256 MiB read and rewritten)", "iters": len(d)}
     if d:
         d.sort()
         res.update(median_us=round(statistics.median(d), 3), p10_us=round(d[len(d) // 10], 3),
@@ -424,6 +425,59 @@ def _compare(got, want, tol):
     err = (got - want).abs()
     bound = tol["atol"] + tol["rtol"] * want.abs()
     return float(err.max()), bool((err <= bound).all())
+
+
+class _on_gpu_local_cpus:
+    """Run the block with this process bound to the CPUs NVML lists as local to GPU
+    ``index`` (so that pinned host memory allocated inside lands on the GPU's NUMA
+    node), then restore the previous binding.  Yields a short description."""
+
+    def __init__(self, index):
+        self.index = index
+        self.saved = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, 16)
+            cpus = {w * 64 + b for w, m in enumerate(words) for b in range(64) if (m >> b) & 1}
+            self.saved = os.sched_getaffinity(0)
+            local = cpus & self.saved
+            if not local:
+                self.saved = None
+                return "no GPU-local CPU available to this process"
+            os.sched_setaffinity(0, local)
+            return f"allocated from the {len(local)} CPUs local to the GPU"
+        except Exception as e:                          # noqa: BLE001
+            self.saved = None
+            return f"GPU-local CPUs unknown ({type(e).__name__})"
+
+    def __exit__(self, *exc):
+        if self.saved is not None:
+            os.sched_setaffinity(0, self.saved)
+        return False
+
+
+def _copy_bandwidth(device, host_src, host_dst, reps=10):
+    """Standalone pinned-host <-> device copy bandwidth (GB/s, CUDA events) of the e2e
+    leg's own buffers: the ceiling that host copies put on the end-to-end number."""
+    dev_a = torch.empty_like(host_src, device=device)
+    dev_b = torch.empty_like(host_dst, device=device)
+    res = {}
+    for name, dst, src in (("h2d_gbs", dev_a, host_src), ("d2h_gbs", host_dst, dev_b)):
+        dst.copy_(src, non_blocking=True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            dst.copy_(src, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize(device)
+        res[name] = round(src.numel() * src.element_size() * reps / (e0.elapsed_time(e1) / 1e3)
+                          / 1e9, 1)
+    return res
 
 
 def _e2e_pipeline(device, world, rank, steps, host_in, dev_in, states, run_step, dev_out,
@@ -596,14 +650,17 @@ def run_b200_arm(args, rank, world, local_rank):
     # ---- end to end through the public API, host buffers in pinned memory ----
     names = ("q", "k", "v", "a", "b")
     local_in = dict(q=q, k=k, v=v, a=a, b=b)
-    host_in = {n: local_in[n].cpu().pin_memory() for n in names}
-    dev_in = [{n: torch.empty_like(local_in[n]) for n in names} for _ in range(2)]
     rows = BATCH // world                       # this rank reads back its batch rows
     r0 = rank * rows
     dev_out = [torch.empty((rows, 1, HV, DIM), dtype=torch.bfloat16, device=device)
                for _ in range(2)]
-    host_out = [torch.empty(dev_out[0].shape, dtype=torch.bfloat16).pin_memory()
-                for _ in range(2)]
+    # pinned host buffers on the GPU's own NUMA node (allocated from its local CPUs)
+    with _on_gpu_local_cpus(local_rank) as numa:
+        host_in = {n: local_in[n].cpu().pin_memory() for n in names}
+        host_out = [torch.empty(dev_out[0].shape, dtype=torch.bfloat16).pin_memory()
+                    for _ in range(2)]
+    dev_in = [{n: torch.empty_like(local_in[n]) for n in names} for _ in range(2)]
+    link = _copy_bandwidth(device, host_in["v"], host_out[0])
     h2d_rank = sum(t.numel() * t.element_size() for t in host_in.values())
     d2h_rank = host_out[0].numel() * host_out[0].element_size()
     if tp is None:
@@ -682,6 +739,7 @@ def run_b200_arm(args, rank, world, local_rank):
                 "h2d_bytes_per_step": h2d_rank * world, "d2h_bytes_per_step": d2h_rank * world,
                 "per_rank": {"h2d": h2d_rank, "d2h": d2h_rank}, "steps": K_e2e, "api": api,
                 "overlap": "H2D / D2H on side streams, double-buffered, ordered by CUDA events",
+                "pinned": numa, "copy_bandwidth": link,
                 "frac_of_value": round(e2e_value / value, 3)},
         "tp_exchange": None if world == 1 else (
             "fused: decode kernel stores outputs into every rank's buffer over NVLink, "
@@ -700,6 +758,13 @@ def run_b200_arm(args, rank, world, local_rank):
         sys.exit(1)
 
 
+def _short_kernel_name(name: str) -> str:
+    """`void (anonymous namespace)::gdn_step_kernel<8, ...>(StepArgs)` -> `gdn_step_kernel`."""
+    import re
+    m = re.search(r"(gdn_\w+|roundtrip_\w+)", name)
+    return m.group(1) if m else name[:60]
+
+
 def run_configs(device, iters):
     """BASELINE's single-GPU configurations 2-4 (plus the bf16-stored state and the
     in-kernel q/k L2-norm) at reduced iterations: CUPTI median per call, algorithmic
@@ -716,16 +781,20 @@ def run_configs(device, iters):
         for _ in range(5):
             fn()
         flushed = state_bytes < 2 * l2
-        # every kernel of this library (gdn_step_kernel, gdn_prefill_chunk_kernel)
-        d = cupti_kernel_durations_us(fn, iters, device, name="gdn_",
-                                      flush=flush_buf.zero_ if flushed else None)
-        d = [x for x in d if x > 0]
-        if not d:                     # no CUPTI records (e.g. under another profiler)
+        # every kernel of this library a call launches (gdn_step_kernel, the prefill
+        # kernels): the median of each, summed over the kernels of one call
+        d = cupti_kernels_by_name(fn, iters, device, flush=flush_buf.bitwise_not_ if flushed else None)
+        per_call = {n: statistics.median(v) for n, v in d.items()
+                    if "gdn_" in n and len(v) >= 0.9 * iters}
+        if not per_call:              # no CUPTI records (e.g. under another profiler)
             return dict(extra, median_us=None, GBps=None, frac=None, l2=None)
-        med = statistics.median(d)
+        med = sum(per_call.values())
         gbs = nbytes / med / 1e3
-        return dict(extra, median_us=round(med, 3), GBps=round(gbs, 1),
-                    frac=round(gbs / peak, 4), l2="flushed" if flushed else "inputs > 2x L2")
+        r = dict(extra, median_us=round(med, 3), GBps=round(gbs, 1),
+                 frac=round(gbs / peak, 4), l2="flushed" if flushed else "inputs > 2x L2")
+        if len(per_call) > 1:
+            r["kernels_us"] = {_short_kernel_name(n): round(t, 3) for n, t in per_call.items()}
+        return r
 
     res = {"peak_gbs": peak, "iters": iters, "decode_batch_sweep": [], "decode_l2norm": [],
            "bf16_state": [], "mtp": []}
@@ -772,7 +841,6 @@ def run_configs(device, iters):
         del inp, out
     # the decode step fused with the layer's gated RMSNorm, against the same step followed
     # by the norm as separate PyTorch kernels (every kernel of a call counted)
-    from gdn_b200.timing import cupti_kernels_by_name
     from oracle import gdn_ref  # the unfused norm below is the oracle's PyTorch ops, on GPU
 
     res["decode_gated_norm"] = []
@@ -797,7 +865,7 @@ def run_configs(device, iters):
         flushed = inp.state.numel() * 4 < 2 * l2
         for _ in range(5):
             unfused()
-        d = cupti_kernels_by_name(unfused, iters, device, flush=flush_buf.zero_ if flushed else None)
+        d = cupti_kernels_by_name(unfused, iters, device, flush=flush_buf.bitwise_not_ if flushed else None)
         per_call = {n: statistics.median(v) for n, v in d.items() if len(v) >= iters}
         r["unfused_us"] = round(sum(per_call.values()), 3) if per_call else None
         r["unfused_kernels_per_call"] = len(per_call)
@@ -808,6 +876,7 @@ def run_configs(device, iters):
     # sequence, 4 q/k and 8 v-heads), a batch of prompts and one long prompt at the
     # Qwen3-Next heads (unit-norm q/k)
     res["prefill"] = []
+    res["prefill_impls"] = []
     for label, lengths, H_, HV_ in PREFILL_CASES:
         d = synthetic.make_prefill_inputs(lengths, H=H_, HV=HV_, seed=11, device=device)
         total, N = sum(lengths), len(lengths)
@@ -822,6 +891,17 @@ def run_configs(device, iters):
             r["tokens_per_s"] = round(total / (r["median_us"] * 1e-6))
             r["ns_per_token_of_longest_sequence"] = round(r["median_us"] * 1e3 / max(lengths), 2)
         res["prefill"].append(r)
+        # the three implementations behind gdn_prefill on the same case: the token loop,
+        # the one-launch chunked kernel and the two-launch chunked form
+        impls = {"token_loop": gdn_b200.prefill_tuned, "chunked_1launch": gdn_b200.prefill_chunked,
+                 "chunked_2launch": gdn_b200.prefill_wy}
+        row = {"case": label}
+        for name, f in impls.items():
+            call = lambda f=f: f(  # noqa: E731
+                d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"],
+                d["cu_seqlens"], d["scale"], out, ns)
+            row[name + "_us"] = measure(call, 1, 2 * ns.numel() * 4, {})["median_us"]
+        res["prefill_impls"].append(row)
         del d, out, ns
     # multi-token speculative verify, B = 64, one intermediate state per token
     for T in (2, 4):
@@ -881,10 +961,9 @@ def run_compare(device, iters, path, group=None):
     kernel and the largest output / state difference is recorded."""
     import gdn_b200
     from gdn_b200 import synthetic
-    from gdn_b200.timing import cupti_kernels_by_name
 
     res = {"method": "CUPTI (torch.profiler), median per kernel summed over the kernels of "
-                     "one call; L2 flushed (256 MiB write) when the state < 2x L2",
+                     "one call; L2 flushed (256 MiB read and rewritten) when the state < 2x L2",
            "iters": iters, "rows": []}
     try:
         from flashinfer.gdn_decode import gated_delta_rule_decode_pretranspose as fi_decode
@@ -907,7 +986,7 @@ def run_compare(device, iters, path, group=None):
             fn()
         torch.cuda.synchronize(device)
         flushed = state_bytes < 2 * l2
-        d = cupti_kernels_by_name(fn, iters, device, flush=flush_buf.zero_ if flushed else None)
+        d = cupti_kernels_by_name(fn, iters, device, flush=flush_buf.bitwise_not_ if flushed else None)
         # kernels seen once per call (CUPTI can drop a few records of a long run)
         per_call = {n: statistics.median(v) for n, v in d.items() if len(v) >= 0.9 * iters}
         total = sum(per_call.values())

@@ -290,10 +290,12 @@ struct TokenRaw {
 //   NVLink, then the ranks meet at a bounded barrier (see the epilogue).
 //   VARLEN (TT == 0, no pool): variable-length prefill; batch entry bi is sequence bi
 //   with tokens cu[bi] .. cu[bi+1]-1 of flat [total, ...] inputs and state slot bi.
-//   GNORM (T = 1, no pool, the CTA holds a whole head): the head's outputs go through
-//   the decode layer's gated RMSNorm before they are stored (see the epilogue).
+//   GNORM (T = 1, no pool): the head's outputs go through the decode layer's gated
+//   RMSNorm before they are stored (see the epilogue).  GNORM == 1: the CTA holds a
+//   whole head.  GNORM == 2: the kDim / kRPC CTAs of a head form a thread-block
+//   cluster and add their partial sums of squares through distributed shared memory.
 template <int LPR, int RG, int W, int TT, bool POOL, bool L2N, bool SCATTER,
-          typename StateT = float, bool VARLEN = false, bool GNORM = false>
+          typename StateT = float, bool VARLEN = false, int GNORM = 0>
 __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   using Chunk = StateChunk<StateT>;
   constexpr int kVec = Chunk::kVec;     // state elements per 16-byte chunk
@@ -308,10 +310,15 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   static_assert(!SCATTER || (TT == 1 && !POOL && kRPC % 8 == 0),
                 "the scatter epilogue moves whole 16-byte chunks of T=1 outputs");
   static_assert(!VARLEN || (TT == 0 && !POOL && !SCATTER), "varlen prefill is multi-token");
-  static_assert(!GNORM || (TT == 1 && !POOL && !SCATTER && !VARLEN && kRPC == kDim),
-                "the gated norm needs a whole head per CTA");
+  static_assert(!GNORM || (TT == 1 && !POOL && !SCATTER && !VARLEN && kRPC <= 32 * W),
+                "the gated norm is a T = 1 epilogue with one thread per output row");
+  static_assert(GNORM != 1 || kRPC == kDim, "GNORM == 1 needs a whole head per CTA");
+  static_assert(GNORM != 2 || (kTPH >= 2 && kTPH <= 8 && kRPC <= 32),
+                "GNORM == 2: a portable cluster of 2..8 CTAs, one warp reduces a CTA's rows");
   __shared__ __align__(16) uint16_t s_out[SCATTER ? kRPC : 1];
-  __shared__ float s_norm[GNORM ? kDim + 1 : 1];
+  // GNORM: [0, kRPC) the CTA's bf16-rounded outputs, [kRPC] its sum of squares
+  // (read by the other CTAs of the cluster), [kRPC + 1] the head's rsqrt
+  __shared__ float s_norm[GNORM ? kRPC + 2 : 1];
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -357,7 +364,37 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
     }
   }
 
-  // ---- state loads first: the only large transfer -------------------------
+  // Offsets into q/k/v/a/b/output fit in 31 bits (checked on the host).
+  auto load_token = [&](int t, TokenRaw<kNC, RG, kVec>& raw) {
+    const int bt = VARLEN ? tok0 + t : bi * T + t;
+    const uint16_t* qp = p.q + (bt * p.H + hq) * kDim + gl * kVec;
+    const uint16_t* kp = p.k + (bt * p.H + hq) * kDim + gl * kVec;
+#pragma unroll
+    for (int c = 0; c < kNC; ++c) {
+      raw.q[c].load(qp + c * LPR * kVec);
+      raw.k[c].load(kp + c * LPR * kVec);
+    }
+    const uint16_t* vp = p.v + (bt * p.HV + hv) * kDim + row0;
+#pragma unroll
+    for (int r = 0; r < RG; ++r) raw.v[r] = __ldg(vp + r * kGroups);
+    raw.a = __ldg(p.a + bt * p.HV + hv);
+    raw.b = __ldg(p.b + bt * p.HV + hv);
+  };
+
+  // Single-token steps outside the tensor-parallel chain fetch the token's q/k/v and
+  // gates before the state: they arrive first, so the gate chain and q.k run while the
+  // state is still in flight (at small batch that latency is the step's critical path).
+  // A chained tensor-parallel step may read only the state before its dependency wait.
+  constexpr bool kTokFirst = TT == 1 && !SCATTER;
+  TokenRaw<kNC, RG, kVec> tok_first;
+  float neg_exp_A = 0.0f, dt_b = 0.0f;
+  if constexpr (kTokFirst) {
+    load_token(0, tok_first);
+    neg_exp_A = neg_exp(__ldg(p.A_log + hv));
+    dt_b = __ldg(p.dt_bias + hv);
+  }
+
+  // ---- state loads: the only large transfer --------------------------------
   // Lane gl holds chunks gl, gl+LPR, ... of each of its rows: element
   // (c*LPR + gl)*kVec + e of the row is h[r][c*kVec + e].
   float h[RG][kEPL];
@@ -379,6 +416,17 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
         Chunk::load(src + r * kGroups * kDim + c * LPR * kVec, &h[r][c * kVec]);
   }
 
+  // GNORM: the gate z and the norm weight of this thread's output row, fetched here so
+  // that their latency hides under the state loads.
+  uint16_t z_raw = 0, w_raw = 0;
+  if constexpr (GNORM != 0) {
+    if (threadIdx.x < kRPC) {
+      const int row = tile_in_head * kRPC + threadIdx.x;
+      z_raw = __ldg(p.z + (static_cast<size_t>(bi) * p.HV + hv) * kDim + row);
+      w_raw = __ldg(p.norm_w + row);
+    }
+  }
+
   if constexpr (SCATTER) {
     // A chained step may start while the previous step's barrier kernel still waits
     // for the other ranks: only the state (last written by a kernel that completed
@@ -390,27 +438,14 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
     if (p.chained) asm volatile("griddepcontrol.wait;" ::: "memory");
   }
 
-  // Offsets into q/k/v/a/b/output fit in 31 bits (checked on the host).
-  auto load_token = [&](int t, TokenRaw<kNC, RG, kVec>& raw) {
-    const int bt = VARLEN ? tok0 + t : bi * T + t;
-    const uint16_t* qp = p.q + (bt * p.H + hq) * kDim + gl * kVec;
-    const uint16_t* kp = p.k + (bt * p.H + hq) * kDim + gl * kVec;
-#pragma unroll
-    for (int c = 0; c < kNC; ++c) {
-      raw.q[c].load(qp + c * LPR * kVec);
-      raw.k[c].load(kp + c * LPR * kVec);
-    }
-    const uint16_t* vp = p.v + (bt * p.HV + hv) * kDim + row0;
-#pragma unroll
-    for (int r = 0; r < RG; ++r) raw.v[r] = __ldg(vp + r * kGroups);
-    raw.a = __ldg(p.a + bt * p.HV + hv);
-    raw.b = __ldg(p.b + bt * p.HV + hv);
-  };
-
   TokenRaw<kNC, RG, kVec> cur;
-  if (!VARLEN || T > 0) load_token(0, cur);
-  const float neg_exp_A = neg_exp(__ldg(p.A_log + hv));
-  const float dt_b = __ldg(p.dt_bias + hv);
+  if constexpr (kTokFirst) {
+    cur = tok_first;
+  } else {
+    if (!VARLEN || T > 0) load_token(0, cur);
+    neg_exp_A = neg_exp(__ldg(p.A_log + hv));
+    dt_b = __ldg(p.dt_bias + hv);
+  }
 
   for (int t = 0; t < T; ++t) {
     TokenRaw<kNC, RG, kVec> nxt;
@@ -515,34 +550,66 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
         Chunk::store(dst + r * kGroups * kDim + c * LPR * kVec, &h[r][c * kVec]);
   }
 
-  if constexpr (GNORM) {
+  if constexpr (GNORM != 0) {
     // Gated RMSNorm of the head's bf16 output o[0..127] (Qwen3-Next's decode layer,
     // transformers models/qwen3_next/modeling_qwen3_next.py:73-82):
     //   x = o * rsqrt(mean(o^2) + eps)   (fp32), rounded to bf16
     //   y = w * x                        (bf16 * bf16, rounded to bf16)
     //   out = y * silu(z)                (fp32), rounded to bf16
     __syncthreads();
-    if (warp == 0) {
-      float ss = 0.0f;
+    if constexpr (GNORM == 1) {
+      if (warp == 0) {
+        float ss = 0.0f;
 #pragma unroll
-      for (int j = 0; j < kDim / 32; ++j) {
-        const float x = s_norm[lane * (kDim / 32) + j];
-        ss = fmaf(x, x, ss);
+        for (int j = 0; j < kDim / 32; ++j) {
+          const float x = s_norm[lane * (kDim / 32) + j];
+          ss = fmaf(x, x, ss);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) s_norm[kRPC + 1] = rsqrtf(ss * (1.0f / kDim) + p.eps);
       }
+      __syncthreads();
+    } else {
+      // The cluster is the kTPH CTAs of this head (cluster rank = tile_in_head).  Each
+      // publishes the sum of squares of its rows; after the cluster barrier every CTA
+      // reads all of them from the others' shared memory.  The second barrier phase
+      // (arrive after the reads, wait before exit) keeps each CTA's shared memory alive
+      // until the other CTAs have read it.
+      if (warp == 0) {
+        const float x = lane < kRPC ? s_norm[lane] : 0.0f;
+        float ss = x * x;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) s_norm[kDim] = rsqrtf(ss * (1.0f / kDim) + p.eps);
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) s_norm[kRPC] = ss;
+      }
+      asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+                   "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+      if (warp == 0) {
+        float ss = 0.0f;
+        if (lane < kTPH) {
+          const uint32_t local = static_cast<uint32_t>(__cvta_generic_to_shared(&s_norm[kRPC]));
+          uint32_t remote;
+          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(lane));
+          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(ss) : "r"(remote) : "memory");
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) s_norm[kRPC + 1] = rsqrtf(ss * (1.0f / kDim) + p.eps);
+      }
+      asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+      __syncthreads();
     }
-    __syncthreads();
-    if (threadIdx.x < kDim && active) {
-      const int row = threadIdx.x;
+    if (threadIdx.x < kRPC) {
+      const int row = tile_in_head * kRPC + threadIdx.x;
       const size_t off = (static_cast<size_t>(bi) * p.HV + hv) * kDim + row;
-      const float x = bf16_to_f32(f32_to_bf16(s_norm[row] * s_norm[kDim]));
-      const float y = bf16_to_f32(f32_to_bf16(bf16_to_f32(__ldg(p.norm_w + row)) * x));
-      const float zf = bf16_to_f32(__ldg(p.z + off));
+      const float x = bf16_to_f32(f32_to_bf16(s_norm[threadIdx.x] * s_norm[kRPC + 1]));
+      const float y = bf16_to_f32(f32_to_bf16(bf16_to_f32(w_raw) * x));
+      const float zf = bf16_to_f32(z_raw);
       const float silu = zf / (1.0f + expf(-zf));
       p.out[off] = f32_to_bf16(y * silu);
     }
+    if constexpr (GNORM == 2) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
 
   if constexpr (SCATTER) {
@@ -708,18 +775,33 @@ LaunchFn pick_bf16_variant(LaunchShape s, bool pool, bool l2n) {
   return l2n ? pick_bf16_shape<TT, false, true>(s) : pick_bf16_shape<TT, false, false>(s);
 }
 
-// Decode step with the gated RMSNorm epilogue: one whole head per CTA (8 lanes per
-// row and 4 rows per lane in 8 warps, or 1 row per lane in 32 warps = 128 rows), with
-// and without the q/k L2-norm.
-// At small batch (few heads, so few CTAs) a head gets 32 warps of 4 rows each, which keeps
-// as many state loads in flight per CTA as the plain step's default split does.
+// Decode step with the gated RMSNorm epilogue, with and without the q/k L2-norm.
+// At small batch (few heads) a head is spread over a cluster of 8 CTAs of 4 warps (the
+// plain step's split: 16 rows per CTA, 8 lanes per row), which keeps as many SMs
+// loading state as the plain step does; the CTAs add their partial sums of squares
+// through distributed shared memory.  At large batch one CTA of 8 warps (4 rows per
+// lane) holds a whole head and the norm needs no cluster.
 template <bool L2N>
 cudaError_t launch_gated_norm(const StepArgs& p, cudaStream_t stream) {
-  const unsigned ctas = static_cast<unsigned>(static_cast<long long>(p.B) * p.HV);
-  if (static_cast<long long>(p.B) * p.HV <= 512)
-    gdn_step_kernel<8, 1, 32, 1, false, L2N, false, float, false, true><<<ctas, 1024, 0, stream>>>(p);
-  else
-    gdn_step_kernel<8, 4, 8, 1, false, L2N, false, float, false, true><<<ctas, 256, 0, stream>>>(p);
+  const long long heads = static_cast<long long>(p.B) * p.HV;
+  if (heads <= 512) {
+    constexpr int kTPH = 8;  // CTAs per head = cluster size
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(heads * kTPH));
+    cfg.blockDim = dim3(128);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kTPH;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gdn_step_kernel<8, 1, 4, 1, false, L2N, false, float, false, 2>,
+                              p);
+  }
+  gdn_step_kernel<8, 4, 8, 1, false, L2N, false, float, false, 1>
+      <<<static_cast<unsigned>(heads), 256, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -1192,22 +1274,55 @@ int gdn_prefill_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, c
   return fn(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
 }
 
+int gdn_prefill_ws(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const float* state,
+                   const float* A_log, const gdn_bf16* a, const float* dt_bias, const gdn_bf16* b,
+                   const int32_t* cu_seqlens, double scale, gdn_bf16* output, float* new_state,
+                   void* workspace, size_t workspace_bytes, int num_seqs, int total_tokens, int H,
+                   int HV, int K, int V, int use_qk_l2norm, void* stream) {
+  // Sequences of 32 tokens or more on average go to the chunked tensor-core path (one
+  // chunk costs about what 15-25 dependent token updates cost in the register-resident
+  // loop); shorter ones, the q/k L2-norm option and inputs without 16-byte alignment stay
+  // on the token loop.  All compute the same recurrence.
+  if (!use_qk_l2norm && num_seqs > 0 && total_tokens >= 32LL * num_seqs &&
+      aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(output, 16)) {
+    if (workspace != nullptr && aligned(workspace, 16) &&
+        workspace_bytes >= gdn_prefill_workspace_bytes(num_seqs, total_tokens, H, HV))
+      return gdn_prefill_wy(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                            new_state, nullptr, workspace, workspace_bytes, num_seqs,
+                            total_tokens, H, HV, K, V, stream);
+    return gdn_prefill_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                               new_state, nullptr, num_seqs, total_tokens, H, HV, K, V, stream);
+  }
+  return gdn_prefill_tuned(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                           new_state, num_seqs, total_tokens, H, HV, K, V, use_qk_l2norm, 0, 0, 0,
+                           stream);
+}
+
 int gdn_prefill(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const float* state,
                 const float* A_log, const gdn_bf16* a, const float* dt_bias, const gdn_bf16* b,
                 const int32_t* cu_seqlens, double scale, gdn_bf16* output, float* new_state,
                 int num_seqs, int total_tokens, int H, int HV, int K, int V, int use_qk_l2norm,
                 void* stream) {
-  // Sequences of 32 tokens or more on average go to the chunked tensor-core kernel (one
-  // chunk costs about what 15-25 dependent token updates cost in the register-resident
-  // loop); shorter ones, the q/k L2-norm option and inputs without 16-byte alignment stay
-  // on the token loop.  Both compute the same recurrence.
-  if (!use_qk_l2norm && num_seqs > 0 && total_tokens >= 32LL * num_seqs &&
-      aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(output, 16))
-    return gdn_prefill_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
-                               new_state, nullptr, num_seqs, total_tokens, H, HV, K, V, stream);
-  return gdn_prefill_tuned(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
-                           new_state, num_seqs, total_tokens, H, HV, K, V, use_qk_l2norm, 0, 0, 0,
-                           stream);
+  const bool chunked = !use_qk_l2norm && num_seqs > 0 && total_tokens >= 32LL * num_seqs &&
+                       H >= 1 && HV >= 1 && aligned(q, 16) && aligned(k, 16) && aligned(v, 16) &&
+                       aligned(output, 16);
+  const size_t need = chunked ? gdn_prefill_workspace_bytes(num_seqs, total_tokens, H, HV) : 0;
+  if (need > 0) {
+    // stream-ordered workspace (capturable; freed after the launches that use it)
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    void* ws = nullptr;
+    if (cudaMallocAsync(&ws, need, st) == cudaSuccess) {
+      const int rc = gdn_prefill_ws(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
+                                    output, new_state, ws, need, num_seqs, total_tokens, H, HV,
+                                    K, V, use_qk_l2norm, stream);
+      const cudaError_t fe = cudaFreeAsync(ws, st);
+      return (rc == GDN_OK && fe != cudaSuccess) ? GDN_ERR_LAUNCH : rc;
+    }
+    (void)cudaGetLastError();   // clear the failed allocation; run without a workspace
+  }
+  return gdn_prefill_ws(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
+                        new_state, nullptr, 0, num_seqs, total_tokens, H, HV, K, V,
+                        use_qk_l2norm, stream);
 }
 
 int gdn_interleave_heads(const gdn_bf16* gathered, gdn_bf16* output, int world, int rows, int HVl,

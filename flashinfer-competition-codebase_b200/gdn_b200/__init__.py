@@ -18,6 +18,7 @@ from .ops import (  # noqa: F401
     interleave_heads,
     kernel_prefill_b200,
     prefill_chunked,
+    prefill_wy,
     prefill_tuned,
     kernel_cuda_b200,
     load_algo_functions,
@@ -32,6 +33,7 @@ __all__ = [
     "gdn_prefill",
     "kernel_prefill_b200",
     "prefill_chunked",
+    "prefill_wy",
     "prefill_tuned",
     "gated_delta_rule_decode_pretranspose",
     "gated_delta_rule_mtp",

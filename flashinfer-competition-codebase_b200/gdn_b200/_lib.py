@@ -17,6 +17,7 @@ _P = ctypes.c_void_p
 _I = ctypes.c_int
 _D = ctypes.c_double
 _U = ctypes.c_uint32
+_Z = ctypes.c_size_t
 
 # Every function declared in include/gdn_b200.h with its ctypes signature.
 SIGNATURES = {
@@ -68,6 +69,17 @@ SIGNATURES = {
     "gdn_prefill_chunked": (
         _I,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P],
+    ),
+    "gdn_prefill_ws": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _Z, _I, _I, _I, _I, _I, _I, _I,
+         _P],
+    ),
+    "gdn_prefill_workspace_bytes": (_Z, [_I, _I, _I, _I]),
+    "gdn_prefill_wy": (
+        _I,
+        [_P, _P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _P, _Z, _I, _I, _I, _I, _I, _I,
+         _P],
     ),
     "gdn_prefill_tuned": (
         _I,
@@ -128,6 +140,11 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
 
 def strerror(code: int) -> str:
     return load().gdn_strerror(code).decode()
+
+
+def prefill_workspace_bytes(num_seqs: int, total_tokens: int, H: int, HV: int) -> int:
+    """Workspace bytes of the two-launch chunked prefill (``gdn_prefill_workspace_bytes``)."""
+    return int(load().gdn_prefill_workspace_bytes(num_seqs, total_tokens, H, HV))
 
 
 def call(name: str, *args) -> None:

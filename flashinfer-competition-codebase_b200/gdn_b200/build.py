@@ -22,13 +22,13 @@ INCLUDE_DIR = os.path.join(os.path.dirname(os.path.dirname(PKG_DIR)), "include")
 LIB_DIR = os.path.join(PKG_DIR, "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200.so")
 
-SOURCES = ["gdn_decode.cu", "gdn_prefill_chunked.cu"]
+SOURCES = ["gdn_decode.cu", "gdn_prefill_chunked.cu", "gdn_prefill_wy.cu"]
 TVM_LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200_tvm.so")
 # measurement-only kernels of the benchmark (the state round-trip floor), kept out of
 # the decode library
 PROBE_LIB_PATH = os.path.join(LIB_DIR, "libgdn_b200_probe.so")
 PROBE_SOURCES = ["roofline_probe.cu"]
-TVM_SOURCES = ["tvm_ffi_entry.cu", "gdn_decode.cu", "gdn_prefill_chunked.cu"]
+TVM_SOURCES = ["tvm_ffi_entry.cu", "gdn_decode.cu", "gdn_prefill_chunked.cu", "gdn_prefill_wy.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-lineinfo",
@@ -54,7 +54,8 @@ def _sources():
 
 
 def _deps():
-    return _sources() + [os.path.join(INCLUDE_DIR, "gdn_b200.h"), os.path.abspath(__file__)]
+    return _sources() + [os.path.join(SRC_DIR, "tc_common.cuh"),
+                         os.path.join(INCLUDE_DIR, "gdn_b200.h"), os.path.abspath(__file__)]
 
 
 def is_stale() -> bool:

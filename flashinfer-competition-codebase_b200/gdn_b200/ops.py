@@ -446,12 +446,21 @@ def kernel_prefill_b200(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
         _check(state, "state", _F32, (N, HV, V, K), dev)
     _check(new_state, "new_state", _F32, (N, HV, V, K), dev)
     _check(output, "output", _BF16, (total, HV, V), dev)
+    # the chunked tensor-core path (sequences of 32+ tokens on average, no q/k L2-norm)
+    # takes its workspace from torch's caching allocator; the C entry decides the path
+    ws = _prefill_workspace(N, total, H, HV, dev) if not use_qk_l2norm and total >= 32 * N else None
     with torch.cuda.device(dev):
         _lib.call(
-            "gdn_prefill", q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(state),
+            "gdn_prefill_ws", q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(state),
             A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), cu.data_ptr(),
-            _resolve_scale(scale, K), output.data_ptr(), new_state.data_ptr(), N, total, H, HV,
-            K, V, int(bool(use_qk_l2norm)), _stream_handle(dev))
+            _resolve_scale(scale, K), output.data_ptr(), new_state.data_ptr(), _ptr(ws),
+            0 if ws is None else ws.numel(), N, total, H, HV, K, V, int(bool(use_qk_l2norm)),
+            _stream_handle(dev))
+
+
+def _prefill_workspace(N: int, total: int, H: int, HV: int, dev) -> Optional[torch.Tensor]:
+    nbytes = _lib.prefill_workspace_bytes(N, total, H, HV)
+    return torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes > 0 else None
 
 
 @torch.no_grad()
@@ -489,6 +498,34 @@ def prefill_chunked(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, out
             A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), cu.data_ptr(),
             _resolve_scale(scale, K), output.data_ptr(), new_state.data_ptr(), status.data_ptr(),
             N, total, H, HV, K, V, _stream_handle(dev))
+    return status
+
+
+@torch.no_grad()
+def prefill_wy(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+               status=None, workspace=None) -> torch.Tensor:
+    """``kernel_prefill_b200`` computed by 64-token chunks in two launches (C entry
+    ``gdn_prefill_wy``): every chunk's state-independent products at once, then each
+    sequence's state chain.  ``workspace`` (uint8, at least
+    ``gdn_prefill_workspace_bytes`` long) is allocated when None.  Returns the int32
+    status tensor (1 if a bounded wait timed out)."""
+    total, H, HV, K, V, N, cu, dev = _check_prefill_inputs(q, k, v, A_log, a, dt_bias, b,
+                                                            cu_seqlens)
+    if state is not None:
+        _check(state, "state", _F32, (N, HV, V, K), dev)
+    _check(new_state, "new_state", _F32, (N, HV, V, K), dev)
+    _check(output, "output", _BF16, (total, HV, V), dev)
+    if workspace is None:
+        workspace = _prefill_workspace(N, total, H, HV, dev)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call(
+            "gdn_prefill_wy", q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(state),
+            A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), cu.data_ptr(),
+            _resolve_scale(scale, K), output.data_ptr(), new_state.data_ptr(), status.data_ptr(),
+            _ptr(workspace), 0 if workspace is None else workspace.numel(), N, total, H, HV, K, V,
+            _stream_handle(dev))
     return status
 
 

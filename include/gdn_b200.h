@@ -238,9 +238,12 @@ GDN_API int gdn_decode_gated_norm(const gdn_bf16* q, const gdn_bf16* k, const gd
  *   output [total_tokens, HV, V] bf16, new_state [num_seqs, HV, V, K] fp32
  * Each sequence runs its tokens in order through the decode recurrence.  When
  * the sequences average 32 tokens or more (and q, k, v, output are 16-byte
- * aligned, use_qk_l2norm == 0) the call runs gdn_prefill_chunked, the chunked
- * tensor-core form of the same recurrence; otherwise a token loop whose state
- * stays in registers for the whole sequence (read once, written once).
+ * aligned, use_qk_l2norm == 0) the call runs gdn_prefill_wy, the chunked
+ * tensor-core form of the same recurrence, with a workspace it allocates
+ * stream-ordered (cudaMallocAsync / cudaFreeAsync on `stream`; if that
+ * allocation fails, the single-launch gdn_prefill_chunked); otherwise a token
+ * loop whose state stays in registers for the whole sequence (read once,
+ * written once).  gdn_prefill_ws takes the workspace from the caller instead.
  * A sequence with no tokens gets a zero final state (the reference's
  * zero-initialised new_state).  Sequence bounds are clamped to
  * [0, total_tokens] on the device, so malformed offsets cannot address memory
@@ -256,7 +259,57 @@ GDN_API int gdn_prefill(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
                         int use_qk_l2norm, void* stream);
 
 /*
- * Variable-length prefill by chunks of 64 tokens on the tensor cores (tcgen05).
+ * gdn_prefill with a caller-provided device workspace (no allocation): the chunked
+ * path uses gdn_prefill_wy when `workspace_bytes` >= gdn_prefill_workspace_bytes(
+ * num_seqs, total_tokens, H, HV), else gdn_prefill_chunked; the token loop uses none
+ * (workspace may then be NULL).  `workspace` must be 16-byte aligned.  Same
+ * reference interface as gdn_prefill.
+ */
+GDN_API int gdn_prefill_ws(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                           const float* state, const float* A_log, const gdn_bf16* a,
+                           const float* dt_bias, const gdn_bf16* b,
+                           const int32_t* cu_seqlens, double scale,
+                           gdn_bf16* output, float* new_state, void* workspace,
+                           size_t workspace_bytes, int num_seqs, int total_tokens, int H,
+                           int HV, int K, int V, int use_qk_l2norm, void* stream);
+
+/*
+ * Device workspace bytes gdn_prefill_wy needs: (num_seqs + ceil(total_tokens / 64))
+ * chunk slots of HV records of 72 KB plus H q images of 32 KB (0 for invalid sizes).
+ * No counterpart in the reference.
+ */
+GDN_API size_t gdn_prefill_workspace_bytes(int num_seqs, int total_tokens, int H, int HV);
+
+/*
+ * Variable-length prefill by chunks of 64 tokens in two launches (tcgen05).
+ *
+ * Same operation, arguments and results as gdn_prefill (the reference's prefill
+ * entries, solution/triton/prefill_kernel.py:11-83, with kernel_prefill_reference's
+ * semantics, :85-183), in the chunked (WY) form of gdn_prefill_chunked, split where
+ * the algebra allows: the first launch computes every chunk's state-independent
+ * products (the triangular solve and the U, W and masked Q K^T tiles) for all chunks of
+ * all sequences at once, one CTA per (chunk, v-head), into `workspace`; the second
+ * runs each (sequence, v-head)'s chain of state-dependent products with the state in
+ * tensor memory.  A long single prompt thus spreads its chunk-local work over the
+ * whole GPU.  q, k, v, the output, the states and the workspace must be 16-byte
+ * aligned; workspace_bytes >= gdn_prefill_workspace_bytes(num_seqs, total_tokens, H, HV).
+ * Sequences must not overlap (non-decreasing cu_seqlens, as the reference assumes):
+ * the chunks of overlapping sequences may share workspace records, which keeps every
+ * access inside the workspace but leaves their results unspecified.  `status` as in
+ * gdn_prefill_chunked.
+ */
+GDN_API int gdn_prefill_wy(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
+                           const float* state, const float* A_log, const gdn_bf16* a,
+                           const float* dt_bias, const gdn_bf16* b,
+                           const int32_t* cu_seqlens, double scale,
+                           gdn_bf16* output, float* new_state, int32_t* status,
+                           void* workspace, size_t workspace_bytes,
+                           int num_seqs, int total_tokens, int H, int HV, int K, int V,
+                           void* stream);
+
+/*
+ * Variable-length prefill by chunks of 64 tokens on the tensor cores (tcgen05), in
+ * one launch and without a workspace.
  *
  * Same operation, arguments and results as gdn_prefill (the reference's prefill
  * entries, solution/triton/prefill_kernel.py:11-83, with kernel_prefill_reference's

@@ -241,3 +241,34 @@ def test_prefill_chunked_rejects(gdn_lib):
     assert call(q=P + 8) == _lib.GDN_ERR_ALIGN        # TMA sources need 16-byte alignment
     assert call(out=P + 2) == _lib.GDN_ERR_ALIGN
     assert call(new_state=P + 4096) == _lib.GDN_ERR_ALIAS
+
+
+def test_prefill_wy_rejects(gdn_lib):
+    f = gdn_lib.gdn_prefill_wy
+    need = gdn_lib.gdn_prefill_workspace_bytes(2, 8, 16, 32)
+    # (N + ceil(total / 64)) slots x (HV records of 72 KB + H q images of 32 KB)
+    assert need == (2 + 1) * (32 * 73728 + 16 * 32768)
+    assert gdn_lib.gdn_prefill_workspace_bytes(-1, 8, 16, 32) == 0
+    assert gdn_lib.gdn_prefill_workspace_bytes(2, 8, 16, 0) == 0
+    base = dict(q=P, k=P, v=P, state=P, A_log=P, a=P, dt_bias=P, b=P, cu=P, scale=0.0,
+                out=P, new_state=P, status=None, ws=P, ws_bytes=need, N=2, total=8, H=16,
+                HV=32, K=128, V=128, stream=None)
+
+    def call(**over):
+        d = dict(base)
+        d.update(over)
+        return f(*d.values())
+
+    # valid except for the one field each call changes: every call fails validation (or
+    # is the N = 0 no-op) before anything is launched
+    assert call(K=64) == _lib.GDN_ERR_SHAPE
+    assert call(N=0, q=None, cu=None, ws=None) == _lib.GDN_OK
+    assert call(cu=None) == _lib.GDN_ERR_NULL
+    assert call(ws=None) == _lib.GDN_ERR_NULL
+    assert call(ws=P + 8) == _lib.GDN_ERR_ALIGN        # bulk copies need 16-byte alignment
+    assert call(q=P + 8) == _lib.GDN_ERR_ALIGN
+    assert call(ws_bytes=need - 16) == _lib.GDN_ERR_SHAPE
+    assert call(new_state=P + 4096) == _lib.GDN_ERR_ALIAS
+    g = gdn_lib.gdn_prefill_ws
+    args = [P] * 9 + [0.0, P, P, P, need, 2, 8, 16, 32, 64, 128, 0, None]   # K = 64
+    assert g(*args) == _lib.GDN_ERR_SHAPE
