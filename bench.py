@@ -80,6 +80,10 @@ PARITY_ENTRIES = (0, 85, 170, 255)        # sampled batch entries checked agains
 PREFILL_CASES = (("contest qk4v8, 1 x 6 tokens (reference prefill workload 0)", [6], 4, 8),
                  ("qwen3next 16/32, 8 x 512 tokens", [512] * 8, 16, 32),
                  ("qwen3next 16/32, 1 x 4096 tokens", [4096], 16, 32))
+# further shapes on which the three prefill implementations are compared (the dispatch rule)
+PREFILL_IMPL_CASES = (("qwen3next 16/32, 64 x 64 tokens", [64] * 64, 16, 32),
+                      ("qwen3next 16/32, 16 x 256 tokens", [256] * 16, 16, 32),
+                      ("qwen3next 16/32, 2 x 2048 tokens", [2048] * 2, 16, 32))
 
 # NVML clock-event reason bits
 _REASONS = {
@@ -877,7 +881,7 @@ def run_configs(device, iters):
     # Qwen3-Next heads (unit-norm q/k)
     res["prefill"] = []
     res["prefill_impls"] = []
-    for label, lengths, H_, HV_ in PREFILL_CASES:
+    for label, lengths, H_, HV_ in PREFILL_CASES + PREFILL_IMPL_CASES:
         d = synthetic.make_prefill_inputs(lengths, H=H_, HV=HV_, seed=11, device=device)
         total, N = sum(lengths), len(lengths)
         out = torch.empty((total, HV_, DIM), dtype=torch.bfloat16, device=device)
@@ -885,12 +889,13 @@ def run_configs(device, iters):
         fn = lambda: gdn_b200.kernel_prefill_b200(  # noqa: E731
             d["q"], d["k"], d["v"], d["state"], d["A_log"], d["a"], d["dt_bias"], d["b"],
             d["cu_seqlens"], d["scale"], out, ns)
-        r = measure(fn, synthetic.prefill_bytes(lengths, H_, HV_), 2 * ns.numel() * 4,
-                    {"case": label, "num_seqs": N, "tokens": total})
-        if r["median_us"]:
-            r["tokens_per_s"] = round(total / (r["median_us"] * 1e-6))
-            r["ns_per_token_of_longest_sequence"] = round(r["median_us"] * 1e3 / max(lengths), 2)
-        res["prefill"].append(r)
+        if (label, lengths, H_, HV_) in PREFILL_CASES:
+            r = measure(fn, synthetic.prefill_bytes(lengths, H_, HV_), 2 * ns.numel() * 4,
+                        {"case": label, "num_seqs": N, "tokens": total})
+            if r["median_us"]:
+                r["tokens_per_s"] = round(total / (r["median_us"] * 1e-6))
+                r["ns_per_token_of_longest_sequence"] = round(r["median_us"] * 1e3 / max(lengths), 2)
+            res["prefill"].append(r)
         # the three implementations behind gdn_prefill on the same case: the token loop,
         # the one-launch chunked kernel and the two-launch chunked form
         impls = {"token_loop": gdn_b200.prefill_tuned, "chunked_1launch": gdn_b200.prefill_chunked,

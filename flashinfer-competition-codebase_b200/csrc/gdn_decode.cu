@@ -1286,7 +1286,7 @@ int gdn_prefill_ws(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, cons
   if (!use_qk_l2norm && num_seqs > 0 && total_tokens >= 32LL * num_seqs &&
       aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(output, 16)) {
     if (workspace != nullptr && aligned(workspace, 16) &&
-        workspace_bytes >= gdn_prefill_workspace_bytes(num_seqs, total_tokens, H, HV))
+        workspace_bytes >= gdn_prefill_workspace_bytes(num_seqs, total_tokens, HV))
       return gdn_prefill_wy(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
                             new_state, nullptr, workspace, workspace_bytes, num_seqs,
                             total_tokens, H, HV, K, V, stream);
@@ -1306,7 +1306,7 @@ int gdn_prefill(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const f
   const bool chunked = !use_qk_l2norm && num_seqs > 0 && total_tokens >= 32LL * num_seqs &&
                        H >= 1 && HV >= 1 && aligned(q, 16) && aligned(k, 16) && aligned(v, 16) &&
                        aligned(output, 16);
-  const size_t need = chunked ? gdn_prefill_workspace_bytes(num_seqs, total_tokens, H, HV) : 0;
+  const size_t need = chunked ? gdn_prefill_workspace_bytes(num_seqs, total_tokens, HV) : 0;
   if (need > 0) {
     // stream-ordered workspace (capturable; freed after the launches that use it)
     cudaStream_t st = static_cast<cudaStream_t>(stream);

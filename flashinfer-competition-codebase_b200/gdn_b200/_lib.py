@@ -75,7 +75,7 @@ SIGNATURES = {
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _Z, _I, _I, _I, _I, _I, _I, _I,
          _P],
     ),
-    "gdn_prefill_workspace_bytes": (_Z, [_I, _I, _I, _I]),
+    "gdn_prefill_workspace_bytes": (_Z, [_I, _I, _I]),
     "gdn_prefill_wy": (
         _I,
         [_P, _P, _P, _P, _P, _P, _P, _P, _P, _D, _P, _P, _P, _P, _Z, _I, _I, _I, _I, _I, _I,
@@ -142,9 +142,9 @@ def strerror(code: int) -> str:
     return load().gdn_strerror(code).decode()
 
 
-def prefill_workspace_bytes(num_seqs: int, total_tokens: int, H: int, HV: int) -> int:
+def prefill_workspace_bytes(num_seqs: int, total_tokens: int, HV: int) -> int:
     """Workspace bytes of the two-launch chunked prefill (``gdn_prefill_workspace_bytes``)."""
-    return int(load().gdn_prefill_workspace_bytes(num_seqs, total_tokens, H, HV))
+    return int(load().gdn_prefill_workspace_bytes(num_seqs, total_tokens, HV))
 
 
 def call(name: str, *args) -> None:

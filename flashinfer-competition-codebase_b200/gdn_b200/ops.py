@@ -448,7 +448,7 @@ def kernel_prefill_b200(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
     _check(output, "output", _BF16, (total, HV, V), dev)
     # the chunked tensor-core path (sequences of 32+ tokens on average, no q/k L2-norm)
     # takes its workspace from torch's caching allocator; the C entry decides the path
-    ws = _prefill_workspace(N, total, H, HV, dev) if not use_qk_l2norm and total >= 32 * N else None
+    ws = _prefill_workspace(N, total, HV, dev) if not use_qk_l2norm and total >= 32 * N else None
     with torch.cuda.device(dev):
         _lib.call(
             "gdn_prefill_ws", q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(state),
@@ -458,8 +458,8 @@ def kernel_prefill_b200(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
             _stream_handle(dev))
 
 
-def _prefill_workspace(N: int, total: int, H: int, HV: int, dev) -> Optional[torch.Tensor]:
-    nbytes = _lib.prefill_workspace_bytes(N, total, H, HV)
+def _prefill_workspace(N: int, total: int, HV: int, dev) -> Optional[torch.Tensor]:
+    nbytes = _lib.prefill_workspace_bytes(N, total, HV)
     return torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes > 0 else None
 
 
@@ -516,7 +516,7 @@ def prefill_wy(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, 
     _check(new_state, "new_state", _F32, (N, HV, V, K), dev)
     _check(output, "output", _BF16, (total, HV, V), dev)
     if workspace is None:
-        workspace = _prefill_workspace(N, total, H, HV, dev)
+        workspace = _prefill_workspace(N, total, HV, dev)
     if status is None:
         status = torch.zeros(1, dtype=torch.int32, device=dev)
     with torch.cuda.device(dev):

@@ -261,7 +261,7 @@ GDN_API int gdn_prefill(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
 /*
  * gdn_prefill with a caller-provided device workspace (no allocation): the chunked
  * path uses gdn_prefill_wy when `workspace_bytes` >= gdn_prefill_workspace_bytes(
- * num_seqs, total_tokens, H, HV), else gdn_prefill_chunked; the token loop uses none
+ * num_seqs, total_tokens, HV), else gdn_prefill_chunked; the token loop uses none
  * (workspace may then be NULL).  `workspace` must be 16-byte aligned.  Same
  * reference interface as gdn_prefill.
  */
@@ -275,10 +275,10 @@ GDN_API int gdn_prefill_ws(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16*
 
 /*
  * Device workspace bytes gdn_prefill_wy needs: (num_seqs + ceil(total_tokens / 64))
- * chunk slots of HV records of 72 KB plus H q images of 32 KB (0 for invalid sizes).
- * No counterpart in the reference.
+ * chunk slots of HV records of 104 KB (0 for invalid sizes).  No counterpart in the
+ * reference.
  */
-GDN_API size_t gdn_prefill_workspace_bytes(int num_seqs, int total_tokens, int H, int HV);
+GDN_API size_t gdn_prefill_workspace_bytes(int num_seqs, int total_tokens, int HV);
 
 /*
  * Variable-length prefill by chunks of 64 tokens in two launches (tcgen05).
@@ -292,7 +292,7 @@ GDN_API size_t gdn_prefill_workspace_bytes(int num_seqs, int total_tokens, int H
  * runs each (sequence, v-head)'s chain of state-dependent products with the state in
  * tensor memory.  A long single prompt thus spreads its chunk-local work over the
  * whole GPU.  q, k, v, the output, the states and the workspace must be 16-byte
- * aligned; workspace_bytes >= gdn_prefill_workspace_bytes(num_seqs, total_tokens, H, HV).
+ * aligned; workspace_bytes >= gdn_prefill_workspace_bytes(num_seqs, total_tokens, HV).
  * Sequences must not overlap (non-decreasing cu_seqlens, as the reference assumes):
  * the chunks of overlapping sequences may share workspace records, which keeps every
  * access inside the workspace but leaves their results unspecified.  `status` as in

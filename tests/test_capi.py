@@ -245,11 +245,10 @@ def test_prefill_chunked_rejects(gdn_lib):
 
 def test_prefill_wy_rejects(gdn_lib):
     f = gdn_lib.gdn_prefill_wy
-    need = gdn_lib.gdn_prefill_workspace_bytes(2, 8, 16, 32)
-    # (N + ceil(total / 64)) slots x (HV records of 72 KB + H q images of 32 KB)
-    assert need == (2 + 1) * (32 * 73728 + 16 * 32768)
-    assert gdn_lib.gdn_prefill_workspace_bytes(-1, 8, 16, 32) == 0
-    assert gdn_lib.gdn_prefill_workspace_bytes(2, 8, 16, 0) == 0
+    need = gdn_lib.gdn_prefill_workspace_bytes(2, 8, 32)
+    assert need == (2 + 1) * 32 * 106496          # (N + ceil(total / 64)) x HV records
+    assert gdn_lib.gdn_prefill_workspace_bytes(-1, 8, 32) == 0
+    assert gdn_lib.gdn_prefill_workspace_bytes(2, 8, 0) == 0
     base = dict(q=P, k=P, v=P, state=P, A_log=P, a=P, dt_bias=P, b=P, cu=P, scale=0.0,
                 out=P, new_state=P, status=None, ws=P, ws_bytes=need, N=2, total=8, H=16,
                 HV=32, K=128, V=128, stream=None)

@@ -143,7 +143,7 @@ def test_overlapping_offsets_stay_inside_the_workspace():
     d["cu_seqlens"] = torch.tensor([0, 200, 10, 300], dtype=torch.int32, device=DEV)
     d["state"] = torch.cat([d["state"]] * 3)
     N, total, HV = 3, 300, 32
-    need = gdn_b200._lib.prefill_workspace_bytes(N, total, 16, HV)
+    need = gdn_b200._lib.prefill_workspace_bytes(N, total, HV)
     buf = torch.full((need + 65536,), 0xA5, dtype=torch.uint8, device=DEV)
     out = torch.empty((total, HV, 128), dtype=torch.bfloat16, device=DEV)
     ns = torch.empty((N, HV, 128, 128), device=DEV)
