@@ -1282,10 +1282,14 @@ int gdn_prefill_ws(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, cons
   // Sequences of 32 tokens or more on average go to the chunked tensor-core path (one
   // chunk costs about what 15-25 dependent token updates cost in the register-resident
   // loop); shorter ones, the q/k L2-norm option and inputs without 16-byte alignment stay
-  // on the token loop.  All compute the same recurrence.
+  // on the token loop.  Among the chunked forms, sequences of 256 tokens or more on
+  // average (4+ chunks) take the two-launch form when a workspace is given (its parallel
+  // first launch pays off once each sequence has several chunks; B200 timings at 16/32
+  // heads: 64 x 64 tokens 224 us one-launch vs 281 us two-launch, 16 x 256 tokens
+  // 177 vs 175 us, 2 x 2048 tokens 301 vs 182 us).  All compute the same recurrence.
   if (!use_qk_l2norm && num_seqs > 0 && total_tokens >= 32LL * num_seqs &&
       aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(output, 16)) {
-    if (workspace != nullptr && aligned(workspace, 16) &&
+    if (total_tokens >= 256LL * num_seqs && workspace != nullptr && aligned(workspace, 16) &&
         workspace_bytes >= gdn_prefill_workspace_bytes(num_seqs, total_tokens, HV))
       return gdn_prefill_wy(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output,
                             new_state, nullptr, workspace, workspace_bytes, num_seqs,
@@ -1303,7 +1307,7 @@ int gdn_prefill(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, const f
                 const int32_t* cu_seqlens, double scale, gdn_bf16* output, float* new_state,
                 int num_seqs, int total_tokens, int H, int HV, int K, int V, int use_qk_l2norm,
                 void* stream) {
-  const bool chunked = !use_qk_l2norm && num_seqs > 0 && total_tokens >= 32LL * num_seqs &&
+  const bool chunked = !use_qk_l2norm && num_seqs > 0 && total_tokens >= 256LL * num_seqs &&
                        H >= 1 && HV >= 1 && aligned(q, 16) && aligned(k, 16) && aligned(v, 16) &&
                        aligned(output, 16);
   const size_t need = chunked ? gdn_prefill_workspace_bytes(num_seqs, total_tokens, HV) : 0;

@@ -60,6 +60,7 @@ struct WyArgs {
   int32_t* status;          // set to 1 if a wait timed out (may be null)
   float scale;
   int N, total, H, HV;
+  int hpc;                  // v-heads per prep CTA (2 when HV / H is even, else 1)
 };
 
 // sequence bounds clamped to [0, total] (a sequence whose end precedes its start is empty)
@@ -74,31 +75,34 @@ __device__ __forceinline__ unsigned char* record(const WyArgs& p, int slot, int 
 }
 
 // =====================================================================================
-// Launch 1: chunk-local products.  256 threads; TMEM lane quarter = warp % 4, the two
-// warps of a quarter split the columns (half = warp / 4).
+// Launch 1: chunk-local products of one chunk slot for `hpc` v-heads that share a q/k
+// head (hpc = 2 when HV / H is even, else 1): the chunk's q/k are loaded and multiplied
+// once, then each v-head's mask, triangular solve and U / W products run in turn.  256
+// threads; TMEM lane quarter = warp % 4, the two warps of a quarter split the columns
+// (half = warp / 4).
 // =====================================================================================
 constexpr int kPT = 256;
+constexpr int kMaxHpc = 2;
 // [Q; K] bf16 K-major 128 x 128: row r (Q rows 0-63, K rows 64-127) at r * 16 of each
 // 2 KB block of 8 features.  Its K rows double as the MN-major K^T operand of W.  After
-// the first product the Q halves (the first 1 KB of each block) hold T diag(beta) (hi in
-// blocks 0-7, lo in blocks 8-15); after the U / W products the whole tile stages W.
+// every head's Q' is written, the Q halves (the first 1 KB of each block) hold the
+// current head's T diag(beta) (hi in blocks 0-7, lo in blocks 8-15).
 constexpr uint32_t kPOffQK = 0;
-constexpr uint32_t kPOffVmn = kPOffQK + 32768;          // V^T bf16 MN-major (v x c)
-// A, then T diag(beta G) (hi, lo; 8 KB each); A and T then stage U (32 KB)
-constexpr uint32_t kPOffA = kPOffVmn + 16384;           // A fp32 [64][kSA]
-constexpr uint32_t kPOffT = kPOffA + 64 * kSA * 4;      // T fp32 [64][kSA]
-// L2, beta, G, then c_j = exp2(L_31 - L_j) and r_t = exp2(L_t - L_31) [64] each
+constexpr uint32_t kPOffVmn = kPOffQK + 32768;              // hpc x V^T bf16 MN-major
+// A, then T diag(beta G) (hi, lo; 8 KB each)
+constexpr uint32_t kPOffA = kPOffVmn + kMaxHpc * 16384;     // A fp32 [64][kSA]
+constexpr uint32_t kPOffT = kPOffA + 64 * kSA * 4;          // T fp32 [64][kSA]
+// per head: L2, beta, G, then c_j = exp2(L_31 - L_j) and r_t = exp2(L_t - L_31) [64] each
 constexpr uint32_t kPOffGate = kPOffT + 64 * kSA * 4;
-constexpr uint32_t kPOffBar = kPOffGate + 320 * 4;      // 4 mbarriers: TMA, P1, U/W, drain
-constexpr uint32_t kPOffMisc = kPOffBar + 4 * 8;        // TMEM base, sequence index
+constexpr uint32_t kPOffBar = kPOffGate + kMaxHpc * 320 * 4;  // 4 mbarriers: TMA, P1, U/W, drain
+constexpr uint32_t kPOffMisc = kPOffBar + 4 * 8;            // TMEM base, sequence index
 constexpr uint32_t kPrepSmem = kPOffMisc + 16;
 static_assert(2 * (kPrepSmem + 1024) <= 233472, "two prep CTAs fit one SM");
-static_assert(2 * 64 * kSA * 4 >= 32768, "A and T together can stage U");
 
 // TMEM (256 columns per CTA, two CTAs per SM)
-constexpr uint32_t kPColP = 0;     // P1 (M = 128): rows 0-63 QK^T, 64-127 KK^T   64
-constexpr uint32_t kPColW = 0;     // W (M = 64, N = 128), after P1 is consumed   128
+constexpr uint32_t kPColW = 0;     // W (M = 64, N = 128)                         128
 constexpr uint32_t kPColU = 128;   // U^T (M = 128, N = 64)                       64
+constexpr uint32_t kPColP = 192;   // P1 (M = 128): rows 0-63 QK^T, 64-127 KK^T   64
 
 constexpr uint32_t kIdP1 = idesc(1, 0, 0, 64, 128);   // [Q;K] K^T
 constexpr uint32_t kIdU = idesc(1, 1, 0, 64, 128);    // V^T (T diag b)^T, A MN-major
@@ -109,7 +113,6 @@ __global__ void __launch_bounds__(kPT, 2)
                        const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_v) {
   extern __shared__ __align__(1024) unsigned char sm[];
-  float* gates = reinterpret_cast<float*>(sm + kPOffGate);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kPOffBar);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + kPOffMisc);
   int* s_seq = reinterpret_cast<int*>(sm + kPOffMisc + 4);
@@ -117,8 +120,10 @@ __global__ void __launch_bounds__(kPT, 2)
   float* sT = reinterpret_cast<float*>(sm + kPOffT);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int slot = blockIdx.x / p.HV;
-  const int hv = blockIdx.x - slot * p.HV;
+  const int hpc = p.hpc;
+  const int groups = p.HV / hpc;
+  const int slot = blockIdx.x / groups;
+  const int hv0 = (blockIdx.x - slot * groups) * hpc;
 
   // which sequence's chunk is this slot (none: a gap of the slot numbering)
   if (tid == 0) *s_seq = -1;
@@ -137,8 +142,7 @@ __global__ void __launch_bounds__(kPT, 2)
   seq_bounds(p, seq, t0, t1);
   const int tc0 = t0 + (slot - seq - (t0 >> 6)) * kC;
   const int nv = min(kC, t1 - tc0);
-  const int hq = hv / (p.HV / p.H);
-  unsigned char* rec = record(p, slot, hv);
+  const int hq = hv0 / (p.HV / p.H);          // the same for every head of this CTA
 
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(bar + i, 1);
@@ -146,15 +150,16 @@ __global__ void __launch_bounds__(kPT, 2)
   }
   __syncthreads();
 
-  // inputs first: 48 TMA boxes of 1 KB (Q and K rows K-major into [Q; K], V^T MN-major);
-  // the tensor memory is allocated while they are in flight
+  // inputs first: TMA boxes of 1 KB (Q and K rows K-major into [Q; K], each head's V^T
+  // MN-major); the tensor memory is allocated while they are in flight
   if (tid == 0) {
     const uint32_t base = smem_u32(sm), mb = smem_u32(bar + 0);
-    mbar_expect_tx(mb, 48 * 1024);
+    mbar_expect_tx(mb, (32 + 16 * hpc) * 1024);
     for (int kc = 0; kc < 16; ++kc) {
       tma_box(base + kPOffQK + kc * 2048, &map_q, hq * kD + kc * 8, tc0, mb);
       tma_box(base + kPOffQK + kc * 2048 + 1024, &map_k, hq * kD + kc * 8, tc0, mb);
-      tma_box(base + kPOffVmn + kc * 1024, &map_v, hv * kD + kc * 8, tc0, mb);
+      for (int h = 0; h < hpc; ++h)
+        tma_box(base + kPOffVmn + h * 16384 + kc * 1024, &map_v, (hv0 + h) * kD + kc * 8, tc0, mb);
     }
   }
   if (warp == 0) {
@@ -162,23 +167,23 @@ __global__ void __launch_bounds__(kPT, 2)
         smem_u32(tmem_slot)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  if (warp == 1) {
+  if (warp >= 1 && warp <= hpc) {
+    // gates of head hv0 + warp - 1
+    const int hv = hv0 + warp - 1;
+    float* g = reinterpret_cast<float*>(sm + kPOffGate) + (warp - 1) * 320;
     const float neg_exp_A = -ex2(__ldg(p.A_log + hv) * kLog2e);
-    chunk_gates(p.a, p.b, p.HV, gates, tc0, nv, hv, neg_exp_A, __ldg(p.dt_bias + hv), lane);
+    chunk_gates(p.a, p.b, p.HV, g, tc0, nv, hv, neg_exp_A, __ldg(p.dt_bias + hv), lane);
     __syncwarp();
     // exp2(L_t - L_j) = r_t c_j around the chunk's middle token (used when the chunk's
     // whole decay range keeps both factors inside the normal fp32 range)
-    const float Lr = gates[31];
+    const float Lr = g[31];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int t = lane * 2 + h;
-      gates[192 + t] = ex2(Lr - gates[t]);
-      gates[256 + t] = ex2(gates[t] - Lr);
+      g[192 + t] = ex2(Lr - g[t]);
+      g[256 + t] = ex2(g[t] - Lr);
     }
   }
-  const float* sL2 = gates;
-  const float* sBeta = gates + 64;
-  const float* sG = gates + 128;
   // the copies are always waited for (bounded), so none is in flight at exit
   bool ok = mbar_wait(bar + 0, 0);
   fence_before();
@@ -193,7 +198,8 @@ __global__ void __launch_bounds__(kPT, 2)
       const uint4 z = make_uint4(0, 0, 0, 0);
       *reinterpret_cast<uint4*>(sm + kPOffQK + c * 2048 + t * 16) = z;
       *reinterpret_cast<uint4*>(sm + kPOffQK + c * 2048 + 1024 + t * 16) = z;
-      *reinterpret_cast<uint4*>(sm + kPOffVmn + c * 1024 + t * 16) = z;
+      for (int h = 0; h < hpc; ++h)
+        *reinterpret_cast<uint4*>(sm + kPOffVmn + h * 16384 + c * 1024 + t * 16) = z;
     }
     fence_async_smem();
     __syncthreads();
@@ -203,7 +209,7 @@ __global__ void __launch_bounds__(kPT, 2)
   const int half = warp >> 2;
   const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
 
-  // ---- P1: [Q; K] K^T -> rows 0-63 QK^T, rows 64-127 KK^T ----
+  // ---- P1: [Q; K] K^T -> rows 0-63 QK^T, rows 64-127 KK^T (shared by the heads) ----
   if (tid == 0 && ok) {
     fence_after();
     const uint32_t qk = smem_u32(sm + kPOffQK);
@@ -213,233 +219,236 @@ __global__ void __launch_bounds__(kPT, 2)
                   sdesc(qk + 64 * 16 + ks * 2 * 2048, 2048, 128), kIdP1, ks > 0);
     mma_commit(bar + 1);
   }
-  // while it runs: Q' = diag(G) Q as the fp32 K-major image of the record
+  // while it runs: every head's Q' = diag(G) Q as the fp32 K-major image of its record
   // (element (t, k) at (k / 4) * 1024 + t * 16)
-  for (int e = tid; e < kC * 16; e += kPT) {
-    const int t = e & 63, kc = e >> 6;
-    const uint4 w = *reinterpret_cast<const uint4*>(sm + kPOffQK + kc * 2048 + t * 16);
-    const float g = sG[t];
-    *reinterpret_cast<float4*>(rec + kRecQp + (2 * kc) * 1024 + t * 16) =
-        make_float4(g * bf16f(w.x & 0xffff), g * bf16f(w.x >> 16), g * bf16f(w.y & 0xffff),
-                    g * bf16f(w.y >> 16));
-    *reinterpret_cast<float4*>(rec + kRecQp + (2 * kc + 1) * 1024 + t * 16) =
-        make_float4(g * bf16f(w.z & 0xffff), g * bf16f(w.z >> 16), g * bf16f(w.w & 0xffff),
-                    g * bf16f(w.w >> 16));
+  for (int h = 0; h < hpc; ++h) {
+    const float* sG = reinterpret_cast<const float*>(sm + kPOffGate) + h * 320 + 128;
+    unsigned char* rec = record(p, slot, hv0 + h);
+    for (int e = tid; e < kC * 16; e += kPT) {
+      const int t = e & 63, kc = e >> 6;
+      const uint4 w = *reinterpret_cast<const uint4*>(sm + kPOffQK + kc * 2048 + t * 16);
+      const float g = sG[t];
+      *reinterpret_cast<float4*>(rec + kRecQp + (2 * kc) * 1024 + t * 16) =
+          make_float4(g * bf16f(w.x & 0xffff), g * bf16f(w.x >> 16), g * bf16f(w.y & 0xffff),
+                      g * bf16f(w.y >> 16));
+      *reinterpret_cast<float4*>(rec + kRecQp + (2 * kc + 1) * 1024 + t * 16) =
+          make_float4(g * bf16f(w.z & 0xffff), g * bf16f(w.z >> 16), g * bf16f(w.w & 0xffff),
+                      g * bf16f(w.w >> 16));
+    }
   }
   if (ok && !mbar_wait(bar + 1, 0)) ok = false;
   fence_after();
-  {
-    // row t = row (QK^T, quarters 0-1) or row - 64 (KK^T, quarters 2-3); this thread's
-    // half of the 64 columns, 8 at a time
-    const int t = row & 63;
-    const float Lt = sL2[t];
-    const float bt = sBeta[t];
-    float x[32];
-    const int j0 = half * 32;
-    tmem_ld32(tmem + kPColP + lane_base + j0, x);
-    auto post = [&](auto decay) {
-#pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) {
-        float v8[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int j = j0 + q8 * 8 + e;
-          v8[e] = (row < 64 ? j <= t : j < t) ? decay(j) * x[q8 * 8 + e] : 0.0f;
-        }
-        const int j = j0 + q8 * 8;
-        if (row < 64) {
-          // QKm[t][j] = exp(L_t - L_j) q_t.k_j, j <= t: bf16 K-major (N = t, K = j)
-          *reinterpret_cast<uint4*>(rec + kRecQKm + (j >> 3) * 1024 + t * 16) =
-              make_uint4(pack2(v8[0], v8[1]), pack2(v8[2], v8[3]), pack2(v8[4], v8[5]),
-                         pack2(v8[6], v8[7]));
-        } else {
-          // A[t][j] = beta_t exp(L_t - L_j) k_t.k_j, j < t
-          float4* dst = reinterpret_cast<float4*>(sA + t * kSA + j);
-          dst[0] = make_float4(bt * v8[0], bt * v8[1], bt * v8[2], bt * v8[3]);
-          dst[1] = make_float4(bt * v8[4], bt * v8[5], bt * v8[6], bt * v8[7]);
-        }
-      }
-    };
-    if (sL2[0] - sL2[63] < 100.0f) {
-      // |L_t - L_31| < 100 for every token: exp2(L_t - L_j) = r_t c_j (two multiplies)
-      const float rt = gates[256 + t];
-      post([&](int j) { return rt * gates[192 + j]; });
-    } else {
-      post([&](int j) { return ex2(Lt - sL2[j]); });
-    }
-  }
-  fence_before();
-  __syncthreads();
+  __syncthreads();          // every head's Q' read the Q rows before T diag(beta) lands there
 
-  // ---- T = (I + A)^-1 on the CUDA cores, by 2 x 2 block inversion ----
-  // [[M11, 0], [M21, M22]]^-1 = [[M11^-1, 0], [-M22^-1 M21 M11^-1, M22^-1]], first for the
-  // four 16 x 16 diagonal blocks (by substitution), then the two 32 x 32 halves, then the
-  // whole; the temporaries live in A's unused upper triangle.
-  // level 1: diagonal blocks D_w (warp w, lane c < 16: column c); upper blocks of T zero
-  if (warp < 4 && lane < 16) {
-    const int bse = warp * 16, c = lane;
-    float x[16];
+  for (int h = 0; h < hpc; ++h) {
+    const float* gates = reinterpret_cast<const float*>(sm + kPOffGate) + h * 320;
+    const float* sL2 = gates;
+    const float* sBeta = gates + 64;
+    const float* sG = gates + 128;
+    unsigned char* rec = record(p, slot, hv0 + h);
+    {
+      // row t = row (QK^T, quarters 0-1) or row - 64 (KK^T, quarters 2-3); this thread's
+      // half of the 64 columns, 8 at a time
+      const int t = row & 63;
+      const float Lt = sL2[t];
+      const float bt = sBeta[t];
+      float x[32];
+      const int j0 = half * 32;
+      tmem_ld32(tmem + kPColP + lane_base + j0, x);
+      auto post = [&](auto decay) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      // the terms of x_0..x_{i-2} first, x_{i-1} (just computed) last: the chain from one
-      // row to the next is one multiply-add
-      float acc = (i == c) ? 1.0f : 0.0f;
-      float acc2 = 0.0f;
+        for (int q8 = 0; q8 < 4; ++q8) {
+          float v8[8];
 #pragma unroll
-      for (int j = 0; j + 1 < i; ++j) {
-        if (j & 1) acc2 -= sA[(bse + i) * kSA + bse + j] * x[j];
-        else acc -= sA[(bse + i) * kSA + bse + j] * x[j];
+          for (int e = 0; e < 8; ++e) {
+            const int j = j0 + q8 * 8 + e;
+            v8[e] = (row < 64 ? j <= t : j < t) ? decay(j) * x[q8 * 8 + e] : 0.0f;
+          }
+          const int j = j0 + q8 * 8;
+          if (row < 64) {
+            // QKm[t][j] = exp(L_t - L_j) q_t.k_j, j <= t: bf16 K-major (N = t, K = j)
+            *reinterpret_cast<uint4*>(rec + kRecQKm + (j >> 3) * 1024 + t * 16) =
+                make_uint4(pack2(v8[0], v8[1]), pack2(v8[2], v8[3]), pack2(v8[4], v8[5]),
+                           pack2(v8[6], v8[7]));
+          } else {
+            // A[t][j] = beta_t exp(L_t - L_j) k_t.k_j, j < t
+            float4* dst = reinterpret_cast<float4*>(sA + t * kSA + j);
+            dst[0] = make_float4(bt * v8[0], bt * v8[1], bt * v8[2], bt * v8[3]);
+            dst[1] = make_float4(bt * v8[4], bt * v8[5], bt * v8[6], bt * v8[7]);
+          }
+        }
+      };
+      if (sL2[0] - sL2[63] < 100.0f) {
+        // |L_t - L_31| < 100 for every token: exp2(L_t - L_j) = r_t c_j (two multiplies)
+        const float rt = gates[256 + t];
+        post([&](int j) { return rt * gates[192 + j]; });
+      } else {
+        post([&](int j) { return ex2(Lt - sL2[j]); });
       }
-      acc += acc2;
-      if (i > 0) acc -= sA[(bse + i) * kSA + bse + i - 1] * x[i - 1];
-      x[i] = (i < c) ? 0.0f : acc;
     }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) sT[(bse + i) * kSA + bse + c] = x[i];
-  }
-  for (int e = tid; e < 64 * 16; e += kPT) {     // float4 slots of the upper blocks
-    const int r = e >> 4, c4 = (e & 15) * 4;
-    if ((c4 >> 4) > (r >> 4))
-      *reinterpret_cast<float4*>(sT + r * kSA + c4) = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  __syncthreads();
-  {
-    // level 2: the 32 x 32 halves.  Thread: block h (0: rows 16-31 / cols 0-15, 1: rows
-    // 48-63 / cols 32-47), row r, columns c, c + 1.
-    const int h = tid >> 7, r = (tid >> 3) & 15, c = (tid & 7) * 2;
-    const int ro = h ? 48 : 16, co = h ? 32 : 0;
-    // P = A_ro,co D_co -> A[co + r][ro + c] (upper triangle)
-    float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const float av = sA[(ro + r) * kSA + co + m];
-      a0 = fmaf(av, sT[(co + m) * kSA + co + c], a0);
-      a1 = fmaf(av, sT[(co + m) * kSA + co + c + 1], a1);
-    }
-    sA[(co + r) * kSA + ro + c] = a0;
-    sA[(co + r) * kSA + ro + c + 1] = a1;
+    fence_before();
     __syncthreads();
-    // T_ro,co = -D_ro P
-    a0 = 0.f; a1 = 0.f;
-#pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const float d = sT[(ro + r) * kSA + ro + m];
-      a0 = fmaf(d, sA[(co + m) * kSA + ro + c], a0);
-      a1 = fmaf(d, sA[(co + m) * kSA + ro + c + 1], a1);
-    }
-    sT[(ro + r) * kSA + co + c] = -a0;
-    sT[(ro + r) * kSA + co + c + 1] = -a1;
-  }
-  __syncthreads();
-  {
-    // level 3: T21 = -T22 A21 T11 (32 x 32 blocks).  Thread: rows i, i + 1; columns j, j + 1.
-    const int i = (tid >> 4) * 2, j = (tid & 15) * 2;
-    // P = A21 T11 -> A[i][32 + j] (upper triangle); T11 holds zeros above its diagonal
-    float p00 = 0.f, p01 = 0.f, p10 = 0.f, p11 = 0.f;
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      const float a0 = sA[(32 + i) * kSA + k], a1 = sA[(33 + i) * kSA + k];
-      const float2 t = *reinterpret_cast<const float2*>(sT + k * kSA + j);
-      p00 = fmaf(a0, t.x, p00); p01 = fmaf(a0, t.y, p01);
-      p10 = fmaf(a1, t.x, p10); p11 = fmaf(a1, t.y, p11);
-    }
-    *reinterpret_cast<float2*>(sA + i * kSA + 32 + j) = make_float2(p00, p01);
-    *reinterpret_cast<float2*>(sA + (i + 1) * kSA + 32 + j) = make_float2(p10, p11);
-    __syncthreads();
-    // T21 = -T22 P; T22 holds zeros above its diagonal
-    p00 = 0.f; p01 = 0.f; p10 = 0.f; p11 = 0.f;
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      const float t0 = sT[(32 + i) * kSA + 32 + k], t1 = sT[(33 + i) * kSA + 32 + k];
-      const float2 pv = *reinterpret_cast<const float2*>(sA + k * kSA + 32 + j);
-      p00 = fmaf(t0, pv.x, p00); p01 = fmaf(t0, pv.y, p01);
-      p10 = fmaf(t1, pv.x, p10); p11 = fmaf(t1, pv.y, p11);
-    }
-    *reinterpret_cast<float2*>(sT + (32 + i) * kSA + j) = make_float2(-p00, -p01);
-    *reinterpret_cast<float2*>(sT + (33 + i) * kSA + j) = make_float2(-p10, -p11);
-  }
-  __syncthreads();
-  // T diag(beta) and T diag(beta G), split hi + lo, as bf16 K-major operands (rows i,
-  // 16-byte chunks of 8 columns j): T diag(beta) into the Q halves of the [Q; K] tile
-  // (block jc at jc * 2048, lo from block 8), T diag(beta G) over A (dead once T is done)
-  for (int e = tid; e < 64 * 8; e += kPT) {
-    const int i = e & 63, jc = e >> 6;
-    const float4 ta = *reinterpret_cast<const float4*>(sT + i * kSA + jc * 8);
-    const float4 tb = *reinterpret_cast<const float4*>(sT + i * kSA + jc * 8 + 4);
-    const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
-    uint32_t bh[4], bl[4], gh[4], gl[4];
-#pragma unroll
-    for (int e2 = 0; e2 < 4; ++e2) {
-      const int j = jc * 8 + 2 * e2;
-      const float x0 = tv[2 * e2] * sBeta[j], x1 = tv[2 * e2 + 1] * sBeta[j + 1];
-      split2(x0, x1, bh[e2], bl[e2]);
-      split2(x0 * sG[j], x1 * sG[j + 1], gh[e2], gl[e2]);
-    }
-    *reinterpret_cast<uint4*>(sm + kPOffQK + jc * 2048 + i * 16) =
-        make_uint4(bh[0], bh[1], bh[2], bh[3]);
-    *reinterpret_cast<uint4*>(sm + kPOffQK + (8 + jc) * 2048 + i * 16) =
-        make_uint4(bl[0], bl[1], bl[2], bl[3]);
-    *reinterpret_cast<uint4*>(sm + kPOffA + jc * 1024 + i * 16) =
-        make_uint4(gh[0], gh[1], gh[2], gh[3]);
-    *reinterpret_cast<uint4*>(sm + kPOffA + 8192 + jc * 1024 + i * 16) =
-        make_uint4(gl[0], gl[1], gl[2], gl[3]);
-  }
-  fence_async_smem();
-  fence_before();
-  __syncthreads();
 
-  // ---- U^T = V^T (T diag b)^T (M = 128) and W = (T diag bG) K (M = 64), hi + lo ----
-  if (tid == 0 && ok) {
-    fence_after();
-    const uint32_t vm = smem_u32(sm + kPOffVmn), qk = smem_u32(sm + kPOffQK);
-    const uint32_t tbg = smem_u32(sm + kPOffA);
+    // ---- T = (I + A)^-1 on the CUDA cores, by 2 x 2 block inversion ----
+    // [[M11, 0], [M21, M22]]^-1 = [[M11^-1, 0], [-M22^-1 M21 M11^-1, M22^-1]], first for the
+    // four 16 x 16 diagonal blocks (by substitution), then the two 32 x 32 halves, then the
+    // whole; the temporaries live in A's unused upper triangle.
+    // level 1: diagonal blocks D_w (warp w, lane c < 16: column c); upper blocks of T zero
+    if (warp < 4 && lane < 16) {
+      const int bse = warp * 16, c = lane;
+      float x[16];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
+      for (int i = 0; i < 16; ++i) {
+        // the terms of x_0..x_{i-2} first, x_{i-1} (just computed) last: the chain from
+        // one row to the next is one multiply-add
+        float acc = (i == c) ? 1.0f : 0.0f;
+        float acc2 = 0.0f;
 #pragma unroll
-      for (int ks = 0; ks < kC / 16; ++ks) {
-        mma_bf16_ss(tmem + kPColU, sdesc(vm + ks * 256, 128, 1024),
-                    sdesc(qk + h * 8 * 2048 + ks * 2 * 2048, 2048, 128), kIdU, h + ks > 0);
-        mma_bf16_ss(tmem + kPColW, sdesc(tbg + h * 8192 + ks * 2 * 1024, 1024, 128),
-                    sdesc(qk + 1024 + ks * 256, 128, 2048), kIdW, h + ks > 0);
+        for (int j = 0; j + 1 < i; ++j) {
+          if (j & 1) acc2 -= sA[(bse + i) * kSA + bse + j] * x[j];
+          else acc -= sA[(bse + i) * kSA + bse + j] * x[j];
+        }
+        acc += acc2;
+        if (i > 0) acc -= sA[(bse + i) * kSA + bse + i - 1] * x[i - 1];
+        x[i] = (i < c) ? 0.0f : acc;
       }
-    }
-    mma_commit(bar + 2);
-  }
-  if (ok && !mbar_wait(bar + 2, 0)) ok = false;
-  fence_after();
-  {
-    float x[32];
-    // U[t][v] fp32 (lane = v) staged over A and T, stored while W is staged
-    const int j0 = half * 32;
-    tmem_ld32(tmem + kPColU + lane_base + j0, x);
-    float* su = reinterpret_cast<float*>(sm + kPOffA);
 #pragma unroll
-    for (int jj = 0; jj < 32; ++jj) su[(j0 + jj) * kD + row] = x[jj];
+      for (int i = 0; i < 16; ++i) sT[(bse + i) * kSA + bse + c] = x[i];
+    }
+    for (int e = tid; e < 64 * 16; e += kPT) {     // float4 slots of the upper blocks
+      const int r = e >> 4, c4 = (e & 15) * 4;
+      if ((c4 >> 4) > (r >> 4))
+        *reinterpret_cast<float4*>(sT + r * kSA + c4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncthreads();
+    {
+      // level 2: the 32 x 32 halves.  Thread: block b2 (0: rows 16-31 / cols 0-15, 1: rows
+      // 48-63 / cols 32-47), row r, columns c, c + 1.
+      const int b2 = tid >> 7, r = (tid >> 3) & 15, c = (tid & 7) * 2;
+      const int ro = b2 ? 48 : 16, co = b2 ? 32 : 0;
+      // P = A_ro,co D_co -> A[co + r][ro + c] (upper triangle)
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const float av = sA[(ro + r) * kSA + co + m];
+        a0 = fmaf(av, sT[(co + m) * kSA + co + c], a0);
+        a1 = fmaf(av, sT[(co + m) * kSA + co + c + 1], a1);
+      }
+      sA[(co + r) * kSA + ro + c] = a0;
+      sA[(co + r) * kSA + ro + c + 1] = a1;
+      __syncthreads();
+      // T_ro,co = -D_ro P
+      a0 = 0.f; a1 = 0.f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        const float d = sT[(ro + r) * kSA + ro + m];
+        a0 = fmaf(d, sA[(co + m) * kSA + ro + c], a0);
+        a1 = fmaf(d, sA[(co + m) * kSA + ro + c + 1], a1);
+      }
+      sT[(ro + r) * kSA + co + c] = -a0;
+      sT[(ro + r) * kSA + co + c + 1] = -a1;
+    }
+    __syncthreads();
+    {
+      // level 3: T21 = -T22 A21 T11 (32 x 32 blocks).  Thread: rows i, i + 1; columns j, j + 1.
+      const int i = (tid >> 4) * 2, j = (tid & 15) * 2;
+      // P = A21 T11 -> A[i][32 + j] (upper triangle); T11 holds zeros above its diagonal
+      float p00 = 0.f, p01 = 0.f, p10 = 0.f, p11 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const float a0 = sA[(32 + i) * kSA + k], a1 = sA[(33 + i) * kSA + k];
+        const float2 t = *reinterpret_cast<const float2*>(sT + k * kSA + j);
+        p00 = fmaf(a0, t.x, p00); p01 = fmaf(a0, t.y, p01);
+        p10 = fmaf(a1, t.x, p10); p11 = fmaf(a1, t.y, p11);
+      }
+      *reinterpret_cast<float2*>(sA + i * kSA + 32 + j) = make_float2(p00, p01);
+      *reinterpret_cast<float2*>(sA + (i + 1) * kSA + 32 + j) = make_float2(p10, p11);
+      __syncthreads();
+      // T21 = -T22 P; T22 holds zeros above its diagonal
+      p00 = 0.f; p01 = 0.f; p10 = 0.f; p11 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const float t0 = sT[(32 + i) * kSA + 32 + k], t1 = sT[(33 + i) * kSA + 32 + k];
+        const float2 pv = *reinterpret_cast<const float2*>(sA + k * kSA + 32 + j);
+        p00 = fmaf(t0, pv.x, p00); p01 = fmaf(t0, pv.y, p01);
+        p10 = fmaf(t1, pv.x, p10); p11 = fmaf(t1, pv.y, p11);
+      }
+      *reinterpret_cast<float2*>(sT + (32 + i) * kSA + j) = make_float2(-p00, -p01);
+      *reinterpret_cast<float2*>(sT + (33 + i) * kSA + j) = make_float2(-p10, -p11);
+    }
+    __syncthreads();
+    // T diag(beta) and T diag(beta G), split hi + lo, as bf16 K-major operands (rows i,
+    // 16-byte chunks of 8 columns j): T diag(beta) into the Q halves of the [Q; K] tile
+    // (block jc at jc * 2048, lo from block 8), T diag(beta G) over A (dead once T is done)
+    for (int e = tid; e < 64 * 8; e += kPT) {
+      const int i = e & 63, jc = e >> 6;
+      const float4 ta = *reinterpret_cast<const float4*>(sT + i * kSA + jc * 8);
+      const float4 tb = *reinterpret_cast<const float4*>(sT + i * kSA + jc * 8 + 4);
+      const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
+      uint32_t bh[4], bl[4], gh[4], gl[4];
+#pragma unroll
+      for (int e2 = 0; e2 < 4; ++e2) {
+        const int j = jc * 8 + 2 * e2;
+        const float x0 = tv[2 * e2] * sBeta[j], x1 = tv[2 * e2 + 1] * sBeta[j + 1];
+        split2(x0, x1, bh[e2], bl[e2]);
+        split2(x0 * sG[j], x1 * sG[j + 1], gh[e2], gl[e2]);
+      }
+      *reinterpret_cast<uint4*>(sm + kPOffQK + jc * 2048 + i * 16) =
+          make_uint4(bh[0], bh[1], bh[2], bh[3]);
+      *reinterpret_cast<uint4*>(sm + kPOffQK + (8 + jc) * 2048 + i * 16) =
+          make_uint4(bl[0], bl[1], bl[2], bl[3]);
+      *reinterpret_cast<uint4*>(sm + kPOffA + jc * 1024 + i * 16) =
+          make_uint4(gh[0], gh[1], gh[2], gh[3]);
+      *reinterpret_cast<uint4*>(sm + kPOffA + 8192 + jc * 1024 + i * 16) =
+          make_uint4(gl[0], gl[1], gl[2], gl[3]);
+    }
     fence_async_smem();
+    fence_before();
     __syncthreads();
-    if (tid == 0) {
-      bulk_store(rec + kRecU, smem_u32(sm + kPOffA), 32768);
-      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    }
-    // W (M = 64 layout: row i = 16 * quarter + lane, lanes 0-15) as the tf32 K-major
-    // image, staged over the [Q; K] tile
-    const int i = (warp & 3) * 16 + lane;
-    for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
-      tmem_ld32(tmem + kPColW + lane_base + c0, x);
-      if (lane < 16) {
+
+    // ---- U^T = V^T (T diag b)^T (M = 128) and W = (T diag bG) K (M = 64), hi + lo ----
+    if (tid == 0 && ok) {
+      fence_after();
+      const uint32_t vm = smem_u32(sm + kPOffVmn + h * 16384), qk = smem_u32(sm + kPOffQK);
+      const uint32_t tbg = smem_u32(sm + kPOffA);
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          *reinterpret_cast<float4*>(sm + kPOffQK + ((c0 >> 2) + q) * 1024 + i * 16) =
-              make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
+      for (int hl = 0; hl < 2; ++hl) {
+#pragma unroll
+        for (int ks = 0; ks < kC / 16; ++ks) {
+          mma_bf16_ss(tmem + kPColU, sdesc(vm + ks * 256, 128, 1024),
+                      sdesc(qk + hl * 8 * 2048 + ks * 2 * 2048, 2048, 128), kIdU, hl + ks > 0);
+          mma_bf16_ss(tmem + kPColW, sdesc(tbg + hl * 8192 + ks * 2 * 1024, 1024, 128),
+                      sdesc(qk + 1024 + ks * 256, 128, 2048), kIdW, hl + ks > 0);
+        }
+      }
+      mma_commit(bar + 2);
+    }
+    if (ok && !mbar_wait(bar + 2, static_cast<uint32_t>(h & 1))) ok = false;
+    fence_after();
+    {
+      float x[32];
+      // U[t][v] fp32 (lane = v): one coalesced 128-byte row piece per column t
+      const int j0 = half * 32;
+      tmem_ld32(tmem + kPColU + lane_base + j0, x);
+      float* up = reinterpret_cast<float*>(rec + kRecU);
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) up[(j0 + jj) * kD + row] = x[jj];
+      // W (M = 64 layout: row i = 16 * quarter + lane, lanes 0-15) as the tf32 K-major
+      // image: 16 consecutive rows' 16-byte pieces per store instruction
+      const int i = (warp & 3) * 16 + lane;
+      for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+        tmem_ld32(tmem + kPColW + lane_base + c0, x);
+        if (lane < 16) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(rec + kRecW + ((c0 >> 2) + q) * 1024 + i * 16) =
+                make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
+        }
       }
     }
-  }
-  fence_async_smem();
-  fence_before();
-  __syncthreads();
-  if (tid == 0) {
-    bulk_store(rec + kRecW, smem_u32(sm + kPOffQK), 32768);
-    bulk_store_drain();
+    // the next head reuses A, T, the Q halves of [Q; K] and the U / W columns
+    fence_before();
+    __syncthreads();
   }
   if (!ok) {
     // a wait timed out: let every product issued finish (bounded) before TMEM is released
@@ -887,6 +896,7 @@ int gdn_prefill_wy(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, cons
   p.status = status;
   p.scale = (scale == 0.0) ? 0.08838834764831845f : static_cast<float>(scale);
   p.N = num_seqs; p.total = total_tokens; p.H = H; p.HV = HV;
+  p.hpc = (HV / H) % 2 == 0 ? 2 : 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CUtensorMap mq{}, mk{}, mv{};
   if (total_tokens > 0) {
@@ -896,7 +906,8 @@ int gdn_prefill_wy(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, cons
     if (cudaFuncSetAttribute(gdn_wy_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kPrepSmem)) != cudaSuccess)
       return GDN_ERR_LAUNCH;
-    gdn_wy_prep_kernel<<<static_cast<unsigned>(slots * HV), kPT, kPrepSmem, st>>>(p, mq, mk, mv);
+    gdn_wy_prep_kernel<<<static_cast<unsigned>(slots * (HV / p.hpc)), kPT, kPrepSmem, st>>>(
+        p, mq, mk, mv);
     if (cudaGetLastError() != cudaSuccess) return GDN_ERR_LAUNCH;
   }
   if (cudaFuncSetAttribute(gdn_wy_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -236,22 +236,6 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
-// One untiled bulk copy this CTA's shared memory -> global (16-byte aligned, bytes a
-// multiple of 16) in the thread's current bulk async-group; the writing threads must
-// have made the source visible to the async proxy (fence_async_smem + a barrier).
-__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
-                   reinterpret_cast<uint64_t>(dst)),
-               "r"(src), "r"(bytes)
-               : "memory");
-}
-// close the thread's bulk async-group and wait until every group has finished reading
-// its shared-memory source
-__device__ __forceinline__ void bulk_store_drain() {
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-
 // ---- gates ---------------------------------------------------------------------------
 // Gates of one chunk by one warp: cumulative log2 decay L (inclusive warp scan), beta
 // and the cumulative decay G = exp2(L) into g[0..63], g[64..127], g[128..191]; tokens

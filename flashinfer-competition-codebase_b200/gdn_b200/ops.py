@@ -446,9 +446,9 @@ def kernel_prefill_b200(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale,
         _check(state, "state", _F32, (N, HV, V, K), dev)
     _check(new_state, "new_state", _F32, (N, HV, V, K), dev)
     _check(output, "output", _BF16, (total, HV, V), dev)
-    # the chunked tensor-core path (sequences of 32+ tokens on average, no q/k L2-norm)
+    # the two-launch chunked path (sequences of 256+ tokens on average, no q/k L2-norm)
     # takes its workspace from torch's caching allocator; the C entry decides the path
-    ws = _prefill_workspace(N, total, HV, dev) if not use_qk_l2norm and total >= 32 * N else None
+    ws = _prefill_workspace(N, total, HV, dev) if not use_qk_l2norm and total >= 256 * N else None
     with torch.cuda.device(dev):
         _lib.call(
             "gdn_prefill_ws", q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(state),

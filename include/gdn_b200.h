@@ -238,12 +238,13 @@ GDN_API int gdn_decode_gated_norm(const gdn_bf16* q, const gdn_bf16* k, const gd
  *   output [total_tokens, HV, V] bf16, new_state [num_seqs, HV, V, K] fp32
  * Each sequence runs its tokens in order through the decode recurrence.  When
  * the sequences average 32 tokens or more (and q, k, v, output are 16-byte
- * aligned, use_qk_l2norm == 0) the call runs gdn_prefill_wy, the chunked
- * tensor-core form of the same recurrence, with a workspace it allocates
- * stream-ordered (cudaMallocAsync / cudaFreeAsync on `stream`; if that
- * allocation fails, the single-launch gdn_prefill_chunked); otherwise a token
- * loop whose state stays in registers for the whole sequence (read once,
- * written once).  gdn_prefill_ws takes the workspace from the caller instead.
+ * aligned, use_qk_l2norm == 0) the call runs the chunked tensor-core form of the
+ * same recurrence: gdn_prefill_wy (two launches) for 256 tokens or more on
+ * average, with a workspace it allocates stream-ordered (cudaMallocAsync /
+ * cudaFreeAsync on `stream`; if that allocation fails, gdn_prefill_chunked), else
+ * the one-launch gdn_prefill_chunked.  Shorter sequences run a token loop whose
+ * state stays in registers for the whole sequence (read once, written once).
+ * gdn_prefill_ws takes the workspace from the caller instead.
  * A sequence with no tokens gets a zero final state (the reference's
  * zero-initialised new_state).  Sequence bounds are clamped to
  * [0, total_tokens] on the device, so malformed offsets cannot address memory
@@ -259,10 +260,10 @@ GDN_API int gdn_prefill(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
                         int use_qk_l2norm, void* stream);
 
 /*
- * gdn_prefill with a caller-provided device workspace (no allocation): the chunked
- * path uses gdn_prefill_wy when `workspace_bytes` >= gdn_prefill_workspace_bytes(
- * num_seqs, total_tokens, HV), else gdn_prefill_chunked; the token loop uses none
- * (workspace may then be NULL).  `workspace` must be 16-byte aligned.  Same
+ * gdn_prefill with a caller-provided device workspace (no allocation): sequences of
+ * 256 tokens or more on average use gdn_prefill_wy when `workspace_bytes` >=
+ * gdn_prefill_workspace_bytes(num_seqs, total_tokens, HV), the other chunked cases
+ * gdn_prefill_chunked; the token loop uses none (workspace may then be NULL).  `workspace` must be 16-byte aligned.  Same
  * reference interface as gdn_prefill.
  */
 GDN_API int gdn_prefill_ws(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,

@@ -95,9 +95,10 @@ def test_matches_the_token_loop_on_a_batch_of_prompts(impl):
 
 
 def test_dispatch_of_the_default_entry_matches_the_oracle():
-    """gdn_prefill picks the chunked kernel for sequences of 32 tokens or more on average
-    and the token loop below; both agree with the oracle."""
-    for lengths in ([80, 40], [5, 9, 2]):
+    """gdn_prefill picks the two-launch chunked form for sequences of 256 tokens or more
+    on average, the one-launch form from 32 tokens, the token loop below; all agree with
+    the oracle."""
+    for lengths in ([300, 260], [80, 40], [5, 9, 2]):
         d = synthetic.make_prefill_inputs(lengths, seed=len(lengths))
         want_o, want_s = gdn_ref.prefill_varlen(d["q"], d["k"], d["v"], d["state"], d["A_log"],
                                                 d["a"], d["dt_bias"], d["b"], d["cu_seqlens"],
@@ -154,3 +155,32 @@ def test_overlapping_offsets_stay_inside_the_workspace():
     assert int(status.item()) == 0
     assert torch.all(buf[need:] == 0xA5)
     assert torch.all(ns[1] == 0)
+
+
+def test_c_entry_allocates_its_workspace_stream_ordered():
+    """The C entry gdn_prefill (no workspace argument) allocates the two-launch form's
+    workspace with cudaMallocAsync on the call's stream and frees it after the launches:
+    two calls in a row agree with the oracle."""
+    import ctypes
+    from gdn_b200 import _lib
+    from gdn_b200.ops import _stream_handle
+
+    d = synthetic.make_prefill_inputs([400, 300], seed=31)
+    want_o, want_s = gdn_ref.prefill_varlen(d["q"], d["k"], d["v"], d["state"], d["A_log"],
+                                            d["a"], d["dt_bias"], d["b"], d["cu_seqlens"],
+                                            d["scale"])
+    g = {n: (t.to(DEV) if isinstance(t, torch.Tensor) else t) for n, t in d.items()}
+    cu = g["cu_seqlens"].to(torch.int32)
+    lib = _lib.load()
+    for _ in range(2):
+        out = torch.full((700, 32, 128), float("nan"), dtype=torch.bfloat16, device=DEV)
+        ns = torch.full((2, 32, 128, 128), float("nan"), device=DEV)
+        rc = lib.gdn_prefill(g["q"].data_ptr(), g["k"].data_ptr(), g["v"].data_ptr(),
+                             g["state"].data_ptr(), g["A_log"].data_ptr(), g["a"].data_ptr(),
+                             g["dt_bias"].data_ptr(), g["b"].data_ptr(), cu.data_ptr(),
+                             ctypes.c_double(float(g["scale"])), out.data_ptr(), ns.data_ptr(),
+                             2, 700, 16, 32, 128, 128, 0, _stream_handle(torch.device(DEV)))
+        assert rc == 0
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float().cpu(), want_o.float(), **OUT_TOL)
+        torch.testing.assert_close(ns.cpu(), want_s, **STATE_TOL)
