@@ -11,6 +11,7 @@
 //   X = S0 W^T,  Delta^T = U^T - X
 //   O^T = scale (S0 Q'^T + Delta^T QKm^T)
 //   S = G_C S0 + Delta^T diag(G_C / G) Kc
+// (X and S0 Q'^T come out of one tf32 product [X | O] = S0 [W; Q']^T.)
 // U, W, Q' and QKm do not depend on the state, so every chunk of every sequence computes
 // them at once in the first launch (gdn_wy_prep_kernel: one CTA per (chunk, v-head), two CTAs
 // per SM) into workspace records.  The second launch (gdn_wy_state_kernel: one CTA per
@@ -21,9 +22,10 @@
 // Workspace record of (chunk slot, v-head), 104 KB, laid out as the shared-memory
 // operand images the second launch copies in with bulk copies:
 //   [0, 8K)      QKm bf16, K-major 64 x 64 (element (t, j) at (j / 8) * 1024 + t * 16 + (j % 8) * 2)
-//   [8K, 40K)    W  fp32 (read as tf32), K-major 64 x 128 (element (t, k) at (k / 4) * 1024 + t * 16 + (k % 4) * 4)
-//   [40K, 72K)   U  fp32, [t][v] row-major
-//   [72K, 104K)  Q' fp32 (read as tf32), K-major 64 x 128, same layout as W
+//   [8K, 72K)    [W; Q'] fp32 (read as tf32), one K-major 128 x 128 operand: W row t (of
+//                64) and Q' row t at rows t and 64 + t (element (r, k) at
+//                (k / 4) * 2048 + r * 16 + (k % 4) * 4)
+//   [72K, 104K)  U  fp32, [t][v] row-major
 // Chunk c of sequence s (tokens [t0, t1) after clamping its offsets to [0, total]) has
 // slot s + floor(t0 / 64) + c: distinct for the chunks of sequences that do not overlap
 // (non-decreasing offsets) and always below N + ceil(total / 64), so the workspace bound
@@ -37,9 +39,8 @@ namespace {
 using namespace gdn_tc;
 
 constexpr uint32_t kRecQKm = 0;
-constexpr uint32_t kRecW = 8192;
-constexpr uint32_t kRecU = 8192 + 32768;
-constexpr uint32_t kRecQp = 8192 + 2 * 32768;
+constexpr uint32_t kRecWQ = 8192;                 // [W; Q'] (W rows, then Q' rows at +1024)
+constexpr uint32_t kRecU = 8192 + 65536;
 constexpr uint32_t kRecBytes = 8192 + 3 * 32768;
 
 constexpr int kSA = 68;     // row stride (floats) of the fp32 A and T scratch
@@ -94,8 +95,9 @@ constexpr uint32_t kPOffA = kPOffVmn + kMaxHpc * 16384;     // A fp32 [64][kSA]
 constexpr uint32_t kPOffT = kPOffA + 64 * kSA * 4;          // T fp32 [64][kSA]
 // per head: L2, beta, G, then c_j = exp2(L_31 - L_j) and r_t = exp2(L_t - L_31) [64] each
 constexpr uint32_t kPOffGate = kPOffT + 64 * kSA * 4;
-constexpr uint32_t kPOffBar = kPOffGate + kMaxHpc * 320 * 4;  // 4 mbarriers: TMA, P1, U/W, drain
-constexpr uint32_t kPOffMisc = kPOffBar + 4 * 8;            // TMEM base, sequence index
+// 5 mbarriers: q/k loads, P1, U/W, drain, v loads
+constexpr uint32_t kPOffBar = kPOffGate + kMaxHpc * 320 * 4;
+constexpr uint32_t kPOffMisc = kPOffBar + 5 * 8;            // TMEM base, sequence index
 constexpr uint32_t kPrepSmem = kPOffMisc + 16;
 static_assert(2 * (kPrepSmem + 1024) <= 233472, "two prep CTAs fit one SM");
 
@@ -145,22 +147,25 @@ __global__ void __launch_bounds__(kPT, 2)
   const int hq = hv0 / (p.HV / p.H);          // the same for every head of this CTA
 
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) mbar_init(bar + i, 1);
+    for (int i = 0; i < 5; ++i) mbar_init(bar + i, 1);
     asm volatile("fence.mbarrier_init.release.cluster;");
   }
   __syncthreads();
 
-  // inputs first: TMA boxes of 1 KB (Q and K rows K-major into [Q; K], each head's V^T
-  // MN-major); the tensor memory is allocated while they are in flight
+  // inputs first: TMA boxes of 1 KB, Q and K rows K-major into [Q; K] (barrier 0, needed
+  // first), each head's V^T MN-major (barrier 4, needed only by the U product); the tensor
+  // memory is allocated while they are in flight
   if (tid == 0) {
-    const uint32_t base = smem_u32(sm), mb = smem_u32(bar + 0);
-    mbar_expect_tx(mb, (32 + 16 * hpc) * 1024);
+    const uint32_t base = smem_u32(sm), mb = smem_u32(bar + 0), mv = smem_u32(bar + 4);
+    mbar_expect_tx(mb, 32 * 1024);
     for (int kc = 0; kc < 16; ++kc) {
       tma_box(base + kPOffQK + kc * 2048, &map_q, hq * kD + kc * 8, tc0, mb);
       tma_box(base + kPOffQK + kc * 2048 + 1024, &map_k, hq * kD + kc * 8, tc0, mb);
-      for (int h = 0; h < hpc; ++h)
-        tma_box(base + kPOffVmn + h * 16384 + kc * 1024, &map_v, (hv0 + h) * kD + kc * 8, tc0, mb);
     }
+    mbar_expect_tx(mv, 16 * 1024 * hpc);
+    for (int kc = 0; kc < 16; ++kc)
+      for (int h = 0; h < hpc; ++h)
+        tma_box(base + kPOffVmn + h * 16384 + kc * 1024, &map_v, (hv0 + h) * kD + kc * 8, tc0, mv);
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(
@@ -198,8 +203,6 @@ __global__ void __launch_bounds__(kPT, 2)
       const uint4 z = make_uint4(0, 0, 0, 0);
       *reinterpret_cast<uint4*>(sm + kPOffQK + c * 2048 + t * 16) = z;
       *reinterpret_cast<uint4*>(sm + kPOffQK + c * 2048 + 1024 + t * 16) = z;
-      for (int h = 0; h < hpc; ++h)
-        *reinterpret_cast<uint4*>(sm + kPOffVmn + h * 16384 + c * 1024 + t * 16) = z;
     }
     fence_async_smem();
     __syncthreads();
@@ -228,10 +231,10 @@ __global__ void __launch_bounds__(kPT, 2)
       const int t = e & 63, kc = e >> 6;
       const uint4 w = *reinterpret_cast<const uint4*>(sm + kPOffQK + kc * 2048 + t * 16);
       const float g = sG[t];
-      *reinterpret_cast<float4*>(rec + kRecQp + (2 * kc) * 1024 + t * 16) =
+      *reinterpret_cast<float4*>(rec + kRecWQ + (2 * kc) * 2048 + 1024 + t * 16) =
           make_float4(g * bf16f(w.x & 0xffff), g * bf16f(w.x >> 16), g * bf16f(w.y & 0xffff),
                       g * bf16f(w.y >> 16));
-      *reinterpret_cast<float4*>(rec + kRecQp + (2 * kc + 1) * 1024 + t * 16) =
+      *reinterpret_cast<float4*>(rec + kRecWQ + (2 * kc + 1) * 2048 + 1024 + t * 16) =
           make_float4(g * bf16f(w.z & 0xffff), g * bf16f(w.z >> 16), g * bf16f(w.w & 0xffff),
                       g * bf16f(w.w >> 16));
     }
@@ -402,6 +405,18 @@ __global__ void __launch_bounds__(kPT, 2)
       *reinterpret_cast<uint4*>(sm + kPOffA + 8192 + jc * 1024 + i * 16) =
           make_uint4(gl[0], gl[1], gl[2], gl[3]);
     }
+    if (h == 0) {
+      // the V^T tiles (always waited for, bounded, so no copy is in flight at exit)
+      if (!mbar_wait(bar + 4, 0)) ok = false;
+      if (nv < kC) {
+        for (int e = tid; e < (kC - nv) * 16 * hpc; e += kPT) {
+          const int hh = e / ((kC - nv) * 16), r = e % ((kC - nv) * 16);
+          const int t = nv + r / 16, c = r % 16;
+          *reinterpret_cast<uint4*>(sm + kPOffVmn + hh * 16384 + c * 1024 + t * 16) =
+              make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
     fence_async_smem();
     fence_before();
     __syncthreads();
@@ -441,7 +456,7 @@ __global__ void __launch_bounds__(kPT, 2)
         if (lane < 16) {
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<float4*>(rec + kRecW + ((c0 >> 2) + q) * 1024 + i * 16) =
+            *reinterpret_cast<float4*>(rec + kRecWQ + ((c0 >> 2) + q) * 2048 + i * 16) =
                 make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
         }
       }
@@ -468,19 +483,18 @@ __global__ void __launch_bounds__(kPT, 2)
 //   warps 8-11   outputs (lane quarter = warp % 4, all 64 columns)
 //   warp 12      producer: gates and the bulk / TMA copies of each chunk's operands
 //   warp 13      tensor-core issue (one lane)
-// Per chunk c:  X = S W^T  ->  Delta pass  (O = S Q'^T runs meanwhile)  ->  state
-// rescale  ->  O += Delta^T QKm^T, S += (Delta f)^T K  ->  X of chunk c + 1, while the
-// output warps convert O of chunk c.  Q' and W are double-buffered (loaded a chunk
-// ahead), O double-buffered in TMEM.
+// Per chunk c:  [X | O] = S [W; Q']^T (one N = 128 product)  ->  Delta pass and state
+// rescale  ->  O += Delta^T QKm^T, S += (Delta f)^T K  ->  [X | O] of chunk c + 1, while
+// the output warps convert O of chunk c.  [W; Q'] is double-buffered (loaded a chunk
+// ahead), [X | O] double-buffered in TMEM.
 // =====================================================================================
 constexpr int kDeltaThreads = 256;
 constexpr int kOutThreads = 128;
 constexpr int kSBlock = kDeltaThreads + kOutThreads + 64;
 constexpr int kWarpOut0 = 8, kWarpProd = 12, kWarpMma = 13;
 
-constexpr uint32_t kSOffW = 0;                       // 2 x W tf32 image 64 x 128    (bulk)
-constexpr uint32_t kSOffQp = kSOffW + 2 * 32768;     // 2 x Q' tf32 image 64 x 128   (bulk)
-constexpr uint32_t kSOffU = kSOffQp + 2 * 32768;     // U fp32 [t][v]                (bulk)
+constexpr uint32_t kSOffWQ = 0;                      // 2 x [W; Q'] tf32 128 x 128    (bulk)
+constexpr uint32_t kSOffU = kSOffWQ + 2 * 65536;     // U fp32 [t][v]                (bulk)
 constexpr uint32_t kSOffQKm = kSOffU + 32768;        // QKm bf16 image 64 x 64       (bulk)
 constexpr uint32_t kSOffKmn = kSOffQKm + 8192;       // K^T bf16 MN-major            (TMA)
 constexpr uint32_t kSOffO = kSOffKmn + 16384;        // output staging bf16 [64][128]
@@ -491,20 +505,19 @@ constexpr uint32_t kStateSmem = kSOffTmem + 16;
 static_assert(kStateSmem <= 227 * 1024, "fits one CTA's shared memory");
 
 // mbarriers (arrival count 1 each)
-constexpr int kBarG1 = 0;        // + (c & 1): Q' and W of chunk c landed
+constexpr int kBarG1 = 0;        // + (c & 1): [W; Q'] of chunk c landed
 constexpr int kBarG2 = 2;        // U and the gates of the chunk landed
 constexpr int kBarG3 = 3;        // QKm and K^T landed
-constexpr int kBarX = 4;         // X done
-constexpr int kBarO = 5;         // O = S Q'^T done (the state may be rescaled)
-constexpr int kBarS34 = 6;       // Delta products done (S and O final for the chunk)
-constexpr int kBarWFree = 7;     // + (c & 1): the products reading Q' / W buffer c & 1 done
-constexpr int kBarUFree = 9;     // U consumed
-constexpr int kBarDelta = 10;    // Delta pass and rescale done
-constexpr int kBarOFree = 11;    // + (c & 1): O buffer c & 1 read out
-constexpr int kBarInit = 13;     // the initial state is in TMEM
-constexpr int kBarDrain = 14;
-constexpr int kNumBars = 15;
-constexpr uint32_t kTxG1 = 2 * 32768;
+constexpr int kBarX = 4;         // [X | O] = S [W; Q']^T done (the state may be rescaled)
+constexpr int kBarS34 = 5;       // Delta products done (S and O final for the chunk)
+constexpr int kBarWFree = 6;     // + (c & 1): the product reading [W; Q'] buffer c & 1 done
+constexpr int kBarUFree = 8;     // U consumed
+constexpr int kBarDelta = 9;     // Delta pass and rescale done
+constexpr int kBarOFree = 10;    // + (c & 1): [X | O] buffer c & 1 read out
+constexpr int kBarInit = 12;     // the initial state is in TMEM
+constexpr int kBarDrain = 13;
+constexpr int kNumBars = 14;
+constexpr uint32_t kTxG1 = 65536;
 constexpr uint32_t kTxG2 = 32768;
 constexpr uint32_t kTxG3 = 8192 + 16384;
 
@@ -514,12 +527,11 @@ constexpr int kEndThreads = kDeltaThreads + kOutThreads + 32;
 
 // TMEM columns (512 allocated)
 constexpr uint32_t kColS = 0;      // state S, fp32 [v][k]                       128
-constexpr uint32_t kColX = 128;    // X = S W^T                                  64
-constexpr uint32_t kColO = 192;    // + 64 (c & 1): O^T (unscaled) of chunk c    2 x 64
-constexpr uint32_t kColDT = 320;   // Delta^T hi / lo bf16 pairs                 64
-constexpr uint32_t kColDF = 384;   // (Delta diag(G_C / G))^T hi / lo            64
+constexpr uint32_t kColXO = 128;   // + 128 (c & 1): [X | O^T (unscaled)] of chunk c  2 x 128
+constexpr uint32_t kColDT = 384;   // Delta^T hi / lo bf16 pairs                 64
+constexpr uint32_t kColDF = 448;   // (Delta diag(G_C / G))^T hi / lo            64
 
-constexpr uint32_t kIdX = idesc(2, 0, 0, 64, 128);    // S W^T, S Q'^T (tf32, A = S in TMEM)
+constexpr uint32_t kIdXO = idesc(2, 0, 0, 128, 128);  // S [W; Q']^T (tf32, A = S in TMEM)
 constexpr uint32_t kIdR = idesc(1, 0, 0, 64, 128);    // Delta^T QKm^T (bf16, A in TMEM)
 constexpr uint32_t kIdK = idesc(1, 0, 1, 128, 128);   // (Delta f)^T K (bf16, A in TMEM, B MN)
 
@@ -563,13 +575,27 @@ __global__ void __launch_bounds__(kSBlock, 1)
     const float dt_b = __ldg(p.dt_bias + hv);
     const uint32_t base = smem_u32(sm);
     bool pok = true;
+    // group 1 of chunk c: [W; Q'] into buffer c & 1, once the product of chunk c - 2 has
+    // read it; issued a chunk ahead (chunk c + 1 during chunk c), the earliest of the
+    // three groups to be free, so that the 64 KB copy lands before it is needed
+    auto load_g1 = [&](int c) {
+      if (c >= 2 && pok)
+        pok = mbar_wait(bar + kBarWFree + (c & 1), static_cast<uint32_t>(((c >> 1) - 1) & 1));
+      if (lane == 0 && pok) {
+        const uint32_t mb = smem_u32(bar + kBarG1 + (c & 1));
+        mbar_expect_tx(mb, kTxG1);
+        bulk_load(base + kSOffWQ + (c & 1) * 65536, record(p, slot0 + c, hv) + kRecWQ, 65536, mb);
+      }
+    };
+    if (nchunks > 0) load_g1(0);
     for (int ch = 0; ch < nchunks; ++ch) {
       const int tc0 = t0 + ch * kC;
       const int nv = min(kC, t1 - tc0);
       const int b = ch & 1;
       const unsigned char* rec = record(p, slot0 + ch, hv);
+      if (ch + 1 < nchunks) load_g1(ch + 1);
       // this chunk's cumulative log2 decay L (inclusive scan, padding without decay) and
-      // f_t = exp2(L_C - L_t), computed before any wait
+      // f_t = exp2(L_C - L_t)
       float l2[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -589,15 +615,6 @@ __global__ void __launch_bounds__(kSBlock, 1)
       }
       const float LC = __shfl_sync(0xffffffffu, s, 31);
       const float f0 = ex2(LC - (s - l2[1])), f1 = ex2(LC - s);
-      // group 1: Q' and W into buffer b, once the products of chunk ch - 2 have read it
-      if (ch >= 2 && pok)
-        pok = mbar_wait(bar + kBarWFree + b, static_cast<uint32_t>(((ch >> 1) - 1) & 1));
-      if (lane == 0 && pok) {
-        const uint32_t mb = smem_u32(bar + kBarG1 + b);
-        mbar_expect_tx(mb, kTxG1);
-        bulk_load(base + kSOffQp + b * 32768, rec + kRecQp, 32768, mb);
-        bulk_load(base + kSOffW + b * 32768, rec + kRecW, 32768, mb);
-      }
       // group 2: the gates (slot b, last read by chunk ch - 2) and U, once chunk ch - 1
       // has consumed its U; the arrival also publishes the gates
       if (ch >= 1 && pok) pok = mbar_wait(bar + kBarUFree, static_cast<uint32_t>((ch - 1) & 1));
@@ -636,36 +653,29 @@ __global__ void __launch_bounds__(kSBlock, 1)
   bool ok = true;
   // ---------------------------------------------------------------- MMA issue ---------
   if (warp == kWarpMma) {
-    const uint32_t tS = tmem + kColS, tX = tmem + kColX;
+    const uint32_t tS = tmem + kColS;
     const uint32_t tDT = tmem + kColDT, tDF = tmem + kColDF;
     if (nchunks > 0 && !mbar_wait(bar + kBarInit, 0)) ok = false;
     for (int ch = 0; ch < nchunks; ++ch) {
       const int tc0 = t0 + ch * kC;
       const int nv = min(kC, t1 - tc0);
       const int b = ch & 1;
-      const uint32_t tO = tmem + kColO + b * 64;
-      // X = S W^T, once the state is final for chunk ch - 1 and W has landed
+      const uint32_t tXO = tmem + kColXO + b * 128;
+      const uint32_t tO = tXO + 64;
+      // [X | O] = S [W; Q']^T into buffer b, once the state is final for chunk ch - 1,
+      // [W; Q'] has landed and the output warps have read buffer b out (chunk ch - 2)
       if (ch >= 1 && ok && !mbar_wait(bar + kBarS34, static_cast<uint32_t>((ch - 1) & 1))) ok = false;
       if (ok && !mbar_wait(bar + kBarG1 + b, static_cast<uint32_t>((ch >> 1) & 1))) ok = false;
-      if (lane == 0 && ok) {
-        fence_after();
-        const uint32_t wm = smem_u32(sm + kSOffW + b * 32768);
-#pragma unroll
-        for (int ks = 0; ks < kD / 8; ++ks)
-          mma_tf32_ts(tX, tS + ks * 8, sdesc(wm + ks * 2048, 1024, 128), kIdX, ks > 0);
-        mma_commit(bar + kBarX);
-      }
-      // O = S Q'^T into buffer b, once the output warps have read it out (chunk ch - 2)
       if (ch >= 2 && ok &&
           !mbar_wait(bar + kBarOFree + b, static_cast<uint32_t>(((ch >> 1) - 1) & 1)))
         ok = false;
       if (lane == 0 && ok) {
         fence_after();
-        const uint32_t qm = smem_u32(sm + kSOffQp + b * 32768);
+        const uint32_t wq = smem_u32(sm + kSOffWQ + b * 65536);
 #pragma unroll
         for (int ks = 0; ks < kD / 8; ++ks)
-          mma_tf32_ts(tO, tS + ks * 8, sdesc(qm + ks * 2048, 1024, 128), kIdX, ks > 0);
-        mma_commit(bar + kBarO);
+          mma_tf32_ts(tXO, tS + ks * 8, sdesc(wq + ks * 2 * 2048, 2048, 128), kIdXO, ks > 0);
+        mma_commit(bar + kBarX);
         mma_commit(bar + kBarWFree + b);
       }
       // Delta products, once QKm / K^T have landed and the Delta pass is done
@@ -722,7 +732,7 @@ __global__ void __launch_bounds__(kSBlock, 1)
       if (ch >= 1 && otid == 0) mbar_arrive(bar + kBarOFree + ((ch - 1) & 1));
       fence_after();
       // O[t][v] = scale * O^T[v][t] (row v = this thread's lane), staged as bf16 rows
-      const uint32_t tO = tmem + kColO + (ch & 1) * 64;
+      const uint32_t tO = tmem + kColXO + (ch & 1) * 128 + 64;
 #pragma unroll
       for (int j0 = 0; j0 < 64; j0 += 32) {
         float x[32];
@@ -749,7 +759,7 @@ __global__ void __launch_bounds__(kSBlock, 1)
   const int row = (warp & 3) * 32 + lane;
   const int half = warp >> 2;
   const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-  const uint32_t tS = tmem + kColS, tX = tmem + kColX;
+  const uint32_t tS = tmem + kColS;
   const uint32_t tDT = tmem + kColDT, tDF = tmem + kColDF;
 
   // initial state: row v into TMEM lane v (fp32), or zeros; an empty sequence ends with
@@ -789,7 +799,7 @@ __global__ void __launch_bounds__(kSBlock, 1)
     {
       float x[32];
       const int j0 = half * 32;
-      tmem_ld32(tX + lane_base + j0, x);
+      tmem_ld32(tmem + kColXO + (ch & 1) * 128 + lane_base + j0, x);
       const float* su = reinterpret_cast<const float*>(sm + kSOffU);
       float dh[16], dl[16], fh[16], fl[16];
 #pragma unroll
@@ -810,9 +820,7 @@ __global__ void __launch_bounds__(kSBlock, 1)
       tmem_st16(tDF + lane_base + (j0 >> 1), fh);
       tmem_st16(tDF + lane_base + 32 + (j0 >> 1), fl);
     }
-    // S <- G_C S, once O = S Q'^T (the last reader of this state) is done
-    if (ok && !mbar_wait(bar + kBarO, par)) ok = false;
-    fence_after();
+    // S <- G_C S ([X | O], the last reader of this state, is done)
     {
       float x[32];
       const float GC = g[64];
