@@ -72,8 +72,8 @@ struct StepArgs {
   uint16_t* peer_out[kMaxRanks];  // [B, hv_total, V] bf16 of each rank, mapped here
   int world, hv0, hv_total;
   // Chained tensor-parallel step (launched as a programmatic dependent of the previous
-  // step's barrier kernel): loads, math and the state store run before
-  // griddepcontrol.wait, the stores into the ranks' output buffers after it.
+  // step's barrier kernel): the state loads run before griddepcontrol.wait, everything
+  // else after it.
   int chained;
   // Gated RMSNorm epilogue (GNORM kernels only): out = bf16(bf16(w * bf16(o * r)) *
   // silu(z)) with r = rsqrt(mean over V of o^2 + eps), o the bf16-rounded head output.
@@ -381,10 +381,11 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
     raw.b = __ldg(p.b + bt * p.HV + hv);
   };
 
-  // Single-token steps fetch the token's q/k/v and gates before the state: they arrive
-  // first, so the gate chain and q.k run while the state is still in flight (at small
-  // batch that latency is the step's critical path).
-  constexpr bool kTokFirst = TT == 1;
+  // Single-token steps outside the tensor-parallel chain fetch the token's q/k/v and
+  // gates before the state: they arrive first, so the gate chain and q.k run while the
+  // state is still in flight (at small batch that latency is the step's critical path).
+  // A chained tensor-parallel step may read only the state before its dependency wait.
+  constexpr bool kTokFirst = TT == 1 && !SCATTER;
   TokenRaw<kNC, RG, kVec> tok_first;
   float neg_exp_A = 0.0f, dt_b = 0.0f;
   if constexpr (kTokFirst) {
@@ -424,6 +425,17 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
       z_raw = __ldg(p.z + (static_cast<size_t>(bi) * p.HV + hv) * kDim + row);
       w_raw = __ldg(p.norm_w + row);
     }
+  }
+
+  if constexpr (SCATTER) {
+    // A chained step may start while the previous step's barrier kernel still waits
+    // for the other ranks: only the state (last written by a kernel that completed
+    // before that barrier started) is read before this point.  The wait returns once
+    // the barrier grid has completed and its memory operations are visible, so the
+    // inputs, the outputs of other ranks and this rank's peer stores below are ordered
+    // after it (the two-buffer rule of the output buffers relies on that).  Without a
+    // programmatic launch the wait returns at once.
+    if (p.chained) asm volatile("griddepcontrol.wait;" ::: "memory");
   }
 
   TokenRaw<kNC, RG, kVec> cur;
@@ -609,14 +621,6 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
     // grid has finished (all of its stores performed).
     constexpr int kChunks = kRPC * 2 / 16;
     __syncthreads();
-    // A chained step may start while the previous step's barrier kernel still waits
-    // for the other ranks: its inputs and state (written by kernels that completed
-    // before that barrier started, never by the step it is chained to) are read, the
-    // math done and the state stored before this point.  The wait returns once the
-    // barrier grid has completed and its memory operations are visible, so the peer
-    // stores below are ordered after it (the two-buffer rule of the output buffers
-    // relies on that).  Without a programmatic launch the wait returns at once.
-    if (p.chained) asm volatile("griddepcontrol.wait;" ::: "memory");
     if (threadIdx.x < p.world * kChunks) {
       const int peer = threadIdx.x / kChunks;
       const int c = threadIdx.x - peer * kChunks;
@@ -639,8 +643,7 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
 // bounded: past timeout_ns it records the failure in *status and gives up.
 __global__ void tp_barrier_kernel(const BarrierArgs p) {
   // Let a chained next step (a programmatic dependent) launch now: its CTAs load their
-  // inputs and state and do their math while this kernel waits, and wait for this grid
-  // before storing into the ranks' output buffers.
+  // state while this kernel waits, and wait for this grid before touching anything else.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ uint32_t s_epoch;
   if (threadIdx.x == 0) s_epoch = *p.epoch + 1u;

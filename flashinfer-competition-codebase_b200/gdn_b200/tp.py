@@ -201,10 +201,6 @@ class TPDecode:
         output buffers, so one graph is recorded per starting buffer and each replay
         picks the one that continues this object's step count (captures and eager
         steps can be mixed).  Every rank must replay the same number of steps.
-        With ``chain`` (the default) every step after the first reads its inputs and
-        state while the previous step's barrier still waits for the other ranks, so no
-        step's inputs may be another step's output within the sequence (a sequence of
-        layers' steps with inputs prepared beforehand, as a decode graph has them).
         Nothing runs while capturing."""
         step_args = list(step_args)
         if not step_args:
@@ -219,8 +215,7 @@ class TPDecode:
                     parity = (start + i) & 1
                     if self.collective == "peer":
                         # steps after the first follow the previous step's barrier kernel
-                        # directly: their decode kernels load, compute and store the state
-                        # while it waits, and store their outputs after it
+                        # directly: their decode kernels start loading state while it waits
                         out = self._peer_step(*args, args[0].shape[0], None, parity=parity,
                                               chained=self.chain and i > 0)
                     else:

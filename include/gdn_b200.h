@@ -392,17 +392,14 @@ GDN_API int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* 
 /*
  * gdn_decode_tp for the next step of a sequence of steps enqueued back to back on
  * one stream (no counterpart in the reference).  The decode kernel is launched as
- * a programmatic dependent of the previous call's barrier kernel: its CTAs read
- * their inputs and state, compute and store the new state while that barrier
- * still waits for the other ranks, and wait for the barrier grid
- * (griddepcontrol.wait) only before storing into the ranks' output buffers.
- * Requires that the kernel enqueued on `stream` right before this call is the
- * barrier of a previous gdn_decode_tp / gdn_decode_tp_chained call (that barrier
- * started only after its own decode kernel, so every state those steps wrote is
- * complete), and therefore that this step's inputs (q, k, v, a, b, A_log,
- * dt_bias, state) are not produced by the step it is chained to or by anything
- * between them: consecutive layers' steps, not a step fed by the previous one's
- * output.  Results are identical to gdn_decode_tp.
+ * a programmatic dependent of the previous call's barrier kernel: its CTAs load
+ * their state while that barrier still waits for the other ranks, and wait for
+ * the barrier grid (griddepcontrol.wait) before reading any other input or
+ * storing any output.  Requires that the kernel enqueued on `stream` right
+ * before this call is the barrier of a previous gdn_decode_tp /
+ * gdn_decode_tp_chained call (that barrier started only after its own decode
+ * kernel, so every state those steps wrote is complete), and that nothing that
+ * writes `state` runs between them.  Results are identical to gdn_decode_tp.
  */
 GDN_API int gdn_decode_tp_chained(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
                                   float* state, const float* A_log, const gdn_bf16* a,
