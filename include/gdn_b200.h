@@ -358,7 +358,9 @@ GDN_API int gdn_prefill_tuned(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf
  * buffer peer_outputs[r] ([B, 1, world*HV, V] bf16, rank r's buffer mapped into
  * this process, e.g. by CUDA IPC or symmetric memory) at this rank's head
  * offset, overlapping the NVLink traffic with the math; a one-CTA barrier
- * kernel enqueued after it then synchronises the ranks through signal words:
+ * kernel enqueued after it (launched as a programmatic dependent of the decode
+ * grid, it waits for that grid to complete) then synchronises the ranks through
+ * signal words:
  * peer_signals[r] points to `world` uint32 words on rank r (zero before the
  * first call); this rank writes the step's epoch into word `rank` of every
  * rank's array and waits until all `world` words of its own array reach it.
@@ -397,9 +399,10 @@ GDN_API int gdn_decode_tp(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* 
  * the barrier grid (griddepcontrol.wait) before reading any other input or
  * storing any output.  Requires that the kernel enqueued on `stream` right
  * before this call is the barrier of a previous gdn_decode_tp /
- * gdn_decode_tp_chained call (that barrier started only after its own decode
- * kernel, so every state those steps wrote is complete), and that nothing that
- * writes `state` runs between them.  Results are identical to gdn_decode_tp.
+ * gdn_decode_tp_chained call (that barrier lets this step launch only after its
+ * own decode kernel has completed, so every state those steps wrote is
+ * complete), and that nothing that writes `state` runs between them.  Results
+ * are identical to gdn_decode_tp.
  */
 GDN_API int gdn_decode_tp_chained(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v,
                                   float* state, const float* A_log, const gdn_bf16* a,
