@@ -13,11 +13,13 @@ value   algorithmic HBM bytes of the whole job per second (GB/s): 4,219,008 B
         the timed steps (CUDA events, max over ranks).  Inputs are resident
         in HBM and larger than L2 (several layers' states updated round robin).
 e2e     the same metric through the public API (``kernel_cuda_b200``; at N > 1
-        the captured ``TPDecode`` step) with every step's inputs (q, k, v, a, b)
+        ``TPDecode.capture_sequence``) with every step's inputs (q, k, v, a, b)
         copied from pinned host memory and its output read back to pinned host
         memory inside the timed region.  Copies run on their own streams, double
         buffered, so step i's kernel overlaps the upload of step i+1 and the
-        read-back of step i-1 (ordered by CUDA events).
+        read-back of step i-1 (ordered by CUDA events); the steps and their copies
+        are recorded as one CUDA graph, so no per-step host work bounds a short
+        step (a 25 us step at N = 8).
 parity  before timing, one eager step and one replayed CUDA-graph step on the same
         seeded inputs (drawn identically on every rank and split by heads at N > 1)
         are compared with the CPU oracle on sampled batch entries: the gathered
@@ -484,45 +486,87 @@ def _copy_bandwidth(device, host_src, host_dst, reps=10):
     return res
 
 
-def _e2e_pipeline(device, world, rank, steps, host_in, dev_in, states, run_step, dev_out,
-                  host_out, out_rows):
-    """``steps`` steps end to end, timed with CUDA events on the launching stream.
+class _E2EHooks:
+    """The end-to-end pipeline around each step, recorded into the graph of the steps.
 
-    Step i uses device input buffer j = i % 2: its H2D copy (side stream) waits until
-    step i-2's kernel has read that buffer; the step waits for its H2D; the step's
-    output rows are read back (side stream) into pinned host memory, and step i+2
-    waits for that read before it writes device output buffer j again.
-    ``run_step(i, j)`` enqueues the step on the current stream and returns the tensor
-    holding this rank's output rows for step i (already in dev_out[j])."""
-    compute = torch.cuda.current_stream(device)
-    s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    ev_h2d = [torch.cuda.Event() for _ in range(2)]
-    ev_kern = [torch.cuda.Event() for _ in range(2)]
-    ev_d2h = [torch.cuda.Event() for _ in range(2)]
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(compute)
-    s_h2d.wait_stream(compute)
-    s_d2h.wait_stream(compute)
-    for i in range(steps):
+    Step i uses device input buffer j = i % 2: its inputs are copied from pinned host
+    memory on a side stream once step i-2's kernel has read that buffer, and the step
+    waits for the copy; the step's output rows are consumed on the step's stream
+    (copied into dev_out[j] when the step returns another tensor, as the tensor-parallel
+    buffer rule asks) and read back into pinned host memory on a second side stream,
+    which step i+2 waits for before it writes dev_out[j] again.  ``before(i)`` and
+    ``after(i, out)`` are called on the capturing stream around step i; step 0 forks
+    the side streams and the last step joins them."""
+
+    def __init__(self, device, steps, host_in, dev_copy, dev_out, host_out, r0=0):
+        self.device, self.steps = device, steps
+        self.host_in, self.dev_copy, self.dev_out, self.host_out = host_in, dev_copy, dev_out, host_out
+        self.r0, self.rows = r0, dev_out[0].shape[0]
+        self.s_h2d, self.s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        self.ev_h2d = [torch.cuda.Event() for _ in range(2)]
+        self.ev_kern = [torch.cuda.Event() for _ in range(2)]
+        self.ev_d2h = [torch.cuda.Event() for _ in range(2)]
+
+    def before(self, i):
+        cur = torch.cuda.current_stream(self.device)
         j = i & 1
-        with torch.cuda.stream(s_h2d):
+        if i == 0:
+            self.s_h2d.wait_stream(cur)
+            self.s_d2h.wait_stream(cur)
+        with torch.cuda.stream(self.s_h2d):
             if i >= 2:
-                s_h2d.wait_event(ev_kern[j])
-            for name, t in host_in.items():
-                dev_in[j][name].copy_(t, non_blocking=True)
-            ev_h2d[j].record(s_h2d)
-        compute.wait_event(ev_h2d[j])
+                self.s_h2d.wait_event(self.ev_kern[j])
+            for name, t in self.host_in.items():
+                self.dev_copy[j][name].copy_(t, non_blocking=True)
+            self.ev_h2d[j].record(self.s_h2d)
+        cur.wait_event(self.ev_h2d[j])
         if i >= 2:
-            compute.wait_event(ev_d2h[j])
-        run_step(i, j)
-        ev_kern[j].record(compute)
-        with torch.cuda.stream(s_d2h):
-            s_d2h.wait_event(ev_kern[j])
-            host_out[j].copy_(dev_out[j], non_blocking=True)
-            ev_d2h[j].record(s_d2h)
-    compute.wait_stream(s_d2h)
-    compute.wait_stream(s_h2d)
-    e1.record(compute)
+            cur.wait_event(self.ev_d2h[j])
+
+    def after(self, i, out):
+        cur = torch.cuda.current_stream(self.device)
+        j = i & 1
+        if out.data_ptr() != self.dev_out[j].data_ptr():
+            self.dev_out[j].copy_(out[self.r0:self.r0 + self.rows])
+        self.ev_kern[j].record(cur)
+        with torch.cuda.stream(self.s_d2h):
+            self.s_d2h.wait_event(self.ev_kern[j])
+            self.host_out[j].copy_(self.dev_out[j], non_blocking=True)
+            self.ev_d2h[j].record(self.s_d2h)
+        if i == self.steps - 1:
+            cur.wait_stream(self.s_d2h)
+            cur.wait_stream(self.s_h2d)
+
+
+class _HookedGraph:
+    """``steps`` calls of ``run_step(i, j)`` (returning the step's output tensor) with
+    the end-to-end hooks around each, recorded as one CUDA graph."""
+
+    def __init__(self, device, steps, run_step, hooks):
+        self.graph = torch.cuda.CUDAGraph()
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.graph(self.graph, stream=stream):
+            for i in range(steps):
+                hooks.before(i)
+                hooks.after(i, run_step(i, i & 1))
+        torch.cuda.current_stream(device).wait_stream(stream)
+
+    def replay(self):
+        self.graph.replay()
+
+
+def _time_replay(device, world, graph):
+    """CUDA-event time (ms) of one replay of ``graph``, after an untimed one."""
+    graph.replay()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    graph.replay()
+    e1.record()
     torch.cuda.synchronize(device)
     return e0.elapsed_time(e1)
 
@@ -683,38 +727,32 @@ def run_b200_arm(args, rank, world, local_rank):
     link = _copy_bandwidth(device, host_pack, host_out[0])
     h2d_rank = sum(t.numel() * t.element_size() for t in local_in.values())
     d2h_rank = host_out[0].numel() * host_out[0].element_size()
+    K_e2e = max(1, min(K, 500))
+    hooks = _E2EHooks(device, K_e2e, host_in, dev_copy, dev_out, host_out, r0=r0)
     if tp is None:
         def run_step(i, j):
             gdn_b200.kernel_cuda_b200(*layer_args(i, [dev_in[j][n] for n in names]),
                                       dev_out[j], states[i % layers])
-        api = "gdn_b200.kernel_cuda_b200 (one call per step)"
-        e2e_graphs = []
+            return dev_out[j]
+        e2e_graph = _HookedGraph(device, K_e2e, run_step, hooks)
+        api = ("gdn_b200.kernel_cuda_b200, one call per step; the steps and their copies "
+               "recorded as one CUDA graph")
     else:
-        # one captured step per (input buffer, layer) pair that the schedule visits
-        period = 2 * layers // math.gcd(2, layers)
-        e2e_graphs = [tp.capture(*layer_args(i, [dev_in[i & 1][n] for n in names]))
-                      for i in range(period)]
-
-        def run_step(i, j):
-            res = e2e_graphs[i % period].replay()
-            dev_out[j].copy_(res[r0:r0 + rows])    # consume before the next step (buffer rule)
-        api = ("gdn_b200.tp.TPDecode.capture (one captured step replayed per step), each "
-               "rank reading back its batch rows of the gathered output")
-    K_e2e = max(1, min(K, 500))
-    _e2e_pipeline(device, world, rank, 4, host_in, dev_copy, states, run_step, dev_out,
-                  host_out, rows)                                   # warm-up, untimed
-    if world > 1:
-        torch.distributed.barrier()
-    e2e_ms = _e2e_pipeline(device, world, rank, K_e2e, host_in, dev_copy, states, run_step,
-                           dev_out, host_out, rows)
-    e2e_ms = max_over_ranks(e2e_ms, world, device)
+        e2e_graph = tp.capture_sequence(
+            [layer_args(i, [dev_in[i & 1][n] for n in names]) for i in range(K_e2e)],
+            before=hooks.before, after=hooks.after)
+        api = ("gdn_b200.tp.TPDecode.capture_sequence with the copies recorded around each "
+               "step (before/after hooks), each rank reading back its batch rows of the "
+               "gathered output")
+    e2e_ms = max_over_ranks(_time_replay(device, world, e2e_graph), world, device)
     e2e_value = total_bytes * K_e2e / (e2e_ms / 1e3) / 1e9
+    del e2e_graph
     # the same pipeline with no step launched: what the host copies alone take per step
     # (next to the device-only step time, it shows whether the copies overlapped)
-    copy_ms = _e2e_pipeline(device, world, rank, K_e2e, host_in, dev_copy, states,
-                            lambda i, j: None, dev_out, host_out, rows)
-    copy_ms = max_over_ranks(copy_ms, world, device)
-    del e2e_graphs
+    copy_hooks = _E2EHooks(device, K_e2e, host_in, dev_copy, dev_out, host_out, r0=r0)
+    copy_graph = _HookedGraph(device, K_e2e, lambda i, j: dev_out[j], copy_hooks)
+    copy_ms = max_over_ranks(_time_replay(device, world, copy_graph), world, device)
+    del copy_graph
 
     latency = b1_latency(device) if (world == 1 and not args.skip_b1) else None
     configs = run_configs(device, args.config_iters) if (world == 1 and not args.skip_configs) \
@@ -763,7 +801,8 @@ def run_b200_arm(args, rank, world, local_rank):
         "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                 "h2d_bytes_per_step": h2d_rank * world, "d2h_bytes_per_step": d2h_rank * world,
                 "per_rank": {"h2d": h2d_rank, "d2h": d2h_rank}, "steps": K_e2e, "api": api,
-                "overlap": "H2D / D2H on side streams, double-buffered, ordered by CUDA events; "
+                "overlap": "H2D / D2H on side streams, double-buffered, ordered by CUDA events, "
+                           "recorded with the steps as one CUDA graph (one replay is timed); "
                            "one packed H2D copy of q/k/v/a/b per step",
                 "pinned": numa, "copy_bandwidth": link,
                 "us_per_step": round(e2e_ms * 1e3 / K_e2e, 2),

@@ -191,7 +191,9 @@ class TPDecode:
         return self.capture_sequence([(q, k, v, state, A_log, a, dt_bias, b, scale)] * steps)
 
     @torch.no_grad()
-    def capture_sequence(self, step_args) -> "CapturedSteps":
+    def capture_sequence(self, step_args, before: Optional[Callable[[int], None]] = None,
+                         after: Optional[Callable[[int, torch.Tensor], None]] = None
+                         ) -> "CapturedSteps":
         """Record one step per entry of ``step_args`` (tuples of the ``step``
         arguments, e.g. one per model layer with that layer's state) as CUDA graphs.
 
@@ -201,10 +203,20 @@ class TPDecode:
         output buffers, so one graph is recorded per starting buffer and each replay
         picks the one that continues this object's step count (captures and eager
         steps can be mixed).  Every rank must replay the same number of steps.
-        Nothing runs while capturing."""
+        Nothing runs while capturing.
+
+        ``before(i)`` and ``after(i, out)``, when given, are called while step i is
+        captured, right before it and right after it, on the capturing stream (current
+        stream): they record work into the same graph, e.g. staging the step's inputs
+        from pinned host memory and reading its output ``out`` back.  ``out`` follows
+        the rule of ``step``: work that reads it must be ordered on the capturing
+        stream before the next step (a copy there, which a side stream may then read).
+        Steps captured with hooks are not chained (the hooks' work sits between one
+        step's barrier and the next step)."""
         step_args = list(step_args)
         if not step_args:
             raise ValueError("nothing to capture")
+        hooked = before is not None or after is not None
         graphs, outs = [], []
         stream = torch.cuda.Stream(self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
@@ -213,13 +225,17 @@ class TPDecode:
             with torch.cuda.graph(g, stream=stream):
                 for i, args in enumerate(step_args):
                     parity = (start + i) & 1
+                    if before is not None:
+                        before(i)
                     if self.collective == "peer":
                         # steps after the first follow the previous step's barrier kernel
                         # directly: their decode kernels start loading state while it waits
                         out = self._peer_step(*args, args[0].shape[0], None, parity=parity,
-                                              chained=self.chain and i > 0)
+                                              chained=self.chain and i > 0 and not hooked)
                     else:
                         out = self.step(*args)
+                    if after is not None:
+                        after(i, out)
             graphs.append(g)
             outs.append(out)
         torch.cuda.current_stream(self.device).wait_stream(stream)

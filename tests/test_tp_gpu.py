@@ -194,7 +194,24 @@ def test_fused_step_replays_from_cuda_graphs():
             torch.cuda.synchronize()
             assert torch.equal(out, want) and torch.equal(g.state, h.state), i
         assert int(tp._epoch.item()) == 13 and tp._steps == 13
-        del steps, many
+        # hooks: an input copy from pinned host memory before each step and a copy of
+        # each step's output after it, recorded into the same graph (steps unchained)
+        q_host = g.q.cpu().pin_memory()
+        got = [torch.empty_like(out) for _ in range(3)]
+        hooked = tp.capture_sequence([g.args()] * 3,
+                                     before=lambda i: g.q.copy_(q_host, non_blocking=True),
+                                     after=lambda i, o: got[i].copy_(o))
+        hooked.replay()
+        wants = []
+        for _ in range(3):
+            want, _ = gdn_b200.gdn_decode(*h.args())
+            wants.append(want.clone())
+        torch.cuda.synchronize()
+        for i in range(3):
+            assert torch.equal(got[i], wants[i]), i
+        assert torch.equal(g.state, h.state)
+        assert int(tp._epoch.item()) == 16 and tp._steps == 16
+        del steps, many, hooked
     finally:
         dist.destroy_process_group()
 
