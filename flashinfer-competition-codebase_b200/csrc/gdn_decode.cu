@@ -316,9 +316,14 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   static_assert(GNORM != 2 || (kTPH >= 2 && kTPH <= 8 && kRPC <= 32),
                 "GNORM == 2: a portable cluster of 2..8 CTAs, one warp reduces a CTA's rows");
   __shared__ __align__(16) uint16_t s_out[SCATTER ? kRPC : 1];
-  // GNORM: [0, kRPC) the CTA's bf16-rounded outputs, [kRPC] its sum of squares
-  // (read by the other CTAs of the cluster), [kRPC + 1] the head's rsqrt
-  __shared__ float s_norm[GNORM ? kRPC + 2 : 1];
+  // GNORM: [0, kRPC) the CTA's bf16-rounded outputs, [kRPC] unused, [kRPC + 1] the
+  // head's rsqrt, [kRPC + 2 + c] (GNORM == 2) the sum of squares of cluster CTA c's rows,
+  // stored there by CTA c
+  __shared__ float s_norm[GNORM ? kRPC + 2 + 8 : 1];
+  // GNORM == 2: the first phase of the cluster barrier, arrived at here and waited on
+  // just before the first store into another CTA's shared memory, establishes that
+  // every CTA of the cluster is running by then.
+  if constexpr (GNORM == 2) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -576,34 +581,33 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
       __syncthreads();
     } else {
       // The cluster is the kTPH CTAs of this head (cluster rank = tile_in_head).  Each
-      // publishes the sum of squares of its rows; after the cluster barrier every CTA
-      // reads all of them from the others' shared memory.  The second barrier phase
-      // (arrive after the reads, wait before exit) keeps each CTA's shared memory alive
-      // until the other CTAs have read it.
+      // stores the sum of squares of its rows into slot kRPC + 2 + tile_in_head of every
+      // CTA's shared memory (its own included); one cluster barrier (release / acquire)
+      // then makes all kTPH partial sums visible to every CTA, which reads its own copy.
+      // No shared memory of another CTA is touched after that barrier, so no CTA waits
+      // for the others before it exits.
+      asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // all CTAs running
       if (warp == 0) {
         const float x = lane < kRPC ? s_norm[lane] : 0.0f;
         float ss = x * x;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) s_norm[kRPC] = ss;
+        if (lane < kTPH) {
+          const uint32_t local =
+              static_cast<uint32_t>(__cvta_generic_to_shared(&s_norm[kRPC + 2 + tile_in_head]));
+          uint32_t remote;
+          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(lane));
+          asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(ss) : "memory");
+        }
       }
       asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
                    "barrier.cluster.wait.acquire.aligned;" ::: "memory");
       if (warp == 0) {
-        float ss = 0.0f;
-        if (lane < kTPH) {
-          const uint32_t local = static_cast<uint32_t>(__cvta_generic_to_shared(&s_norm[kRPC]));
-          uint32_t remote;
-          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(lane));
-          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(ss) : "r"(remote) : "memory");
-        }
+        float ss = lane < kTPH ? s_norm[kRPC + 2 + lane] : 0.0f;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (lane == 0) s_norm[kRPC + 1] = rsqrtf(ss * (1.0f / kDim) + p.eps);
       }
-      // (relaxed: the remote loads above have completed, their values are in use; no
-      // memory needs ordering for the other CTAs)
-      asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
       __syncthreads();
     }
     if (threadIdx.x < kRPC) {
@@ -615,7 +619,6 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
       const float silu = zf / (1.0f + expf(-zf));
       p.out[off] = f32_to_bf16(y * silu);
     }
-    if constexpr (GNORM == 2) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
 
   if constexpr (SCATTER) {
