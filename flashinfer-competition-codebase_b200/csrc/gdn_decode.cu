@@ -320,10 +320,22 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   // head's rsqrt, [kRPC + 2 + c] (GNORM == 2) the sum of squares of cluster CTA c's rows,
   // stored there by CTA c
   __shared__ float s_norm[GNORM ? kRPC + 2 + 8 : 1];
-  // GNORM == 2: the first phase of the cluster barrier, arrived at here and waited on
-  // just before the first store into another CTA's shared memory, establishes that
-  // every CTA of the cluster is running by then.
-  if constexpr (GNORM == 2) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  // GNORM == 2: an mbarrier that completes once all kTPH partial sums have landed here
+  // (each CTA's st.async carries 4 bytes of transaction count).  It is initialised and
+  // armed before the cluster barrier's one phase, which is arrived at here and waited on
+  // just before the first store into another CTA, so every CTA is running and has armed
+  // its mbarrier by then.
+  __shared__ __align__(8) uint64_t s_nbar[GNORM == 2 ? 1 : 1];
+  if constexpr (GNORM == 2) {
+    if (threadIdx.x == 0) {
+      const uint32_t nb = static_cast<uint32_t>(__cvta_generic_to_shared(s_nbar));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(nb) : "memory");
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(nb),
+                   "r"(static_cast<uint32_t>(kTPH * 4)) : "memory");
+    }
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  }
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -581,12 +593,14 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
       __syncthreads();
     } else {
       // The cluster is the kTPH CTAs of this head (cluster rank = tile_in_head).  Each
-      // stores the sum of squares of its rows into slot kRPC + 2 + tile_in_head of every
-      // CTA's shared memory (its own included); one cluster barrier (release / acquire)
-      // then makes all kTPH partial sums visible to every CTA, which reads its own copy.
-      // No shared memory of another CTA is touched after that barrier, so no CTA waits
-      // for the others before it exits.
-      asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // all CTAs running
+      // sends the sum of squares of its rows to slot kRPC + 2 + tile_in_head of every
+      // CTA's shared memory (its own included) with st.async, which completes 4 bytes of
+      // the receiving CTA's mbarrier transaction count; each CTA waits on its own
+      // mbarrier and reads its own copy.  No cluster-scope fence is involved, and a CTA
+      // exits only after every partial sum addressed to it has landed.  The wait is
+      // bounded (it cannot run out while every CTA of the cluster runs, which the
+      // cluster launch guarantees); if it ever did, the head's outputs would be NaN.
+      asm volatile("barrier.cluster.wait.aligned;" ::: "memory");   // all CTAs armed
       if (warp == 0) {
         const float x = lane < kRPC ? s_norm[lane] : 0.0f;
         float ss = x * x;
@@ -595,18 +609,23 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
         if (lane < kTPH) {
           const uint32_t local =
               static_cast<uint32_t>(__cvta_generic_to_shared(&s_norm[kRPC + 2 + tile_in_head]));
-          uint32_t remote;
+          const uint32_t lbar = static_cast<uint32_t>(__cvta_generic_to_shared(s_nbar));
+          uint32_t remote, rbar;
           asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(lane));
-          asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(ss) : "memory");
+          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(lbar), "r"(lane));
+          asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+                       ::"r"(remote), "r"(__float_as_uint(ss)), "r"(rbar) : "memory");
         }
-      }
-      asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-                   "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-      if (warp == 0) {
-        float ss = lane < kTPH ? s_norm[kRPC + 2 + lane] : 0.0f;
+        const uint32_t nb = static_cast<uint32_t>(__cvta_generic_to_shared(s_nbar));
+        uint32_t done = 0;
+        for (int it = 0; it < (1 << 22) && !done; ++it) {
+          asm volatile("{\n.reg .pred p;\nmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n"
+                       "selp.u32 %0, 1, 0, p;\n}" : "=r"(done) : "r"(nb) : "memory");
+        }
+        float tot = (done && lane < kTPH) ? s_norm[kRPC + 2 + lane] : 0.0f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        if (lane == 0) s_norm[kRPC + 1] = rsqrtf(ss * (1.0f / kDim) + p.eps);
+        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+        if (lane == 0) s_norm[kRPC + 1] = done ? rsqrtf(tot * (1.0f / kDim) + p.eps) : __int_as_float(0x7fc00000);
       }
       __syncthreads();
     }
