@@ -450,8 +450,8 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
 
   if constexpr (SCATTER) {
     // A chained step may start while the previous step's barrier kernel still waits
-    // for the other ranks: only the state (last written by a kernel that completed
-    // before that barrier started) is read before this point.  The wait returns once
+    // for the other ranks: only the state (last written by a decode grid that had
+    // completed before that barrier let this grid launch) is read before this point.  The wait returns once
     // the barrier grid has completed and its memory operations are visible, so the
     // inputs, the outputs of other ranks and this rank's peer stores below are ordered
     // after it (the two-buffer rule of the output buffers relies on that).  Without a
@@ -643,8 +643,9 @@ __global__ void __launch_bounds__(W * 32) gdn_step_kernel(const StepArgs p) {
   if constexpr (SCATTER) {
     // The CTA's kRPC outputs (one head, rows tile_in_head*kRPC ...) go to every
     // rank's output buffer as 16-byte NVLink stores, overlapping the other CTAs'
-    // math.  Completion is established by tp_barrier_kernel, which runs after this
-    // grid has finished (all of its stores performed).
+    // math.  Completion is established by tp_barrier_kernel, which signals the other
+    // ranks only after its griddepcontrol.wait has seen this grid finish (all of its
+    // stores performed).
     constexpr int kChunks = kRPC * 2 / 16;
     __syncthreads();
     if (threadIdx.x < p.world * kChunks) {
