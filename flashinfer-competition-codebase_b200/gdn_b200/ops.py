@@ -421,9 +421,13 @@ def _check_prefill_inputs(q, k, v, A_log, a, dt_bias, b, cu_seqlens):
         raise TypeError(f"cu_seqlens must be int32 or int64, got {cu_seqlens.dtype}")
     if cu_seqlens.device != dev:
         raise ValueError(f"cu_seqlens is on {cu_seqlens.device}, expected {dev}")
-    # int64 offsets are clamped into [0, total] before narrowing (no host sync); the
-    # kernel clamps every sequence's bounds into the same range
-    cu = cu_seqlens.clamp(0, total).to(torch.int32).contiguous()
+    # Every prefill kernel clamps each sequence's bounds into [0, total] itself, so int32
+    # offsets go to it as they are (no extra launch); int64 offsets are clamped into the
+    # same range before narrowing (no host sync), so that none wraps into a valid one
+    if cu_seqlens.dtype == torch.int32:
+        cu = cu_seqlens.contiguous()
+    else:
+        cu = cu_seqlens.clamp(0, total).to(torch.int32).contiguous()
     return total, H, HV, K, V, cu.numel() - 1, cu, dev
 
 
