@@ -69,6 +69,24 @@ def test_int64_indices_cannot_wrap_onto_a_valid_slot():
     assert same.tolist() == [0, 3]
 
 
+def test_prefill_offsets_int32_pass_through_int64_clamped(monkeypatch):
+    """int32 sequence offsets reach the kernels as they are (the kernels clamp each
+    sequence's bounds into [0, total] themselves, so no extra launch is spent); int64
+    offsets are clamped into [0, total] before narrowing, so that 2**32 + 3 cannot wrap
+    onto token 3.  (The per-tensor check, which refuses CPU tensors, is stubbed: only the
+    offsets logic is under test here.)"""
+    monkeypatch.setattr(ops, "_check", lambda *a, **k: None)
+    x = synthetic.make_prefill_inputs([3, 5])
+    args = (x["q"], x["k"], x["v"], x["A_log"], x["a"], x["dt_bias"], x["b"])
+    cu32 = torch.tensor([0, 3, 8], dtype=torch.int32)
+    total, H, HV, K, V, N, cu, _ = ops._check_prefill_inputs(*args, cu32)
+    assert (total, H, HV, N) == (8, 16, 32, 2)
+    assert cu.data_ptr() == cu32.data_ptr()            # the caller's tensor, untouched
+    cu64 = torch.tensor([-5, 2**32 + 3, 8], dtype=torch.int64)
+    *_, cu, _ = ops._check_prefill_inputs(*args, cu64)
+    assert cu.dtype == torch.int32 and cu.tolist() == [0, 8, 8]
+
+
 def test_scale_default():
     assert ops._resolve_scale(None, 128) == 1 / math.sqrt(128)
     assert ops._resolve_scale(0.0, 128) == 1 / math.sqrt(128)
