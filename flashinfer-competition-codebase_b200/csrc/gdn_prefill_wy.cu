@@ -122,6 +122,9 @@ __global__ void __launch_bounds__(kPT, 2)
   float* sT = reinterpret_cast<float*>(sm + kPOffT);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // the state kernel is this grid's programmatic dependent: it may launch once every CTA
+  // here has started, and reads no record before this grid has completed
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int hpc = p.hpc;
   const int groups = p.HV / hpc;
   const int slot = blockIdx.x / groups;
@@ -570,6 +573,11 @@ __global__ void __launch_bounds__(kSBlock, 1)
 
   // ---------------------------------------------------------------- producer ----------
   if (warp == kWarpProd) {
+    // Launched as a programmatic dependent of the prep kernel: the other warps allocate
+    // TMEM and load the initial state while the prep grid finishes; the records are read
+    // (by this warp only) once it has completed and its stores are visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
     // waits bounded; after a failed wait nothing more is issued
     const float neg_exp_A = -ex2(__ldg(p.A_log + hv) * kLog2e);
     const float dt_b = __ldg(p.dt_bias + hv);
@@ -921,8 +929,20 @@ int gdn_prefill_wy(const gdn_bf16* q, const gdn_bf16* k, const gdn_bf16* v, cons
   if (cudaFuncSetAttribute(gdn_wy_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(kStateSmem)) != cudaSuccess)
     return GDN_ERR_LAUNCH;
-  gdn_wy_state_kernel<<<static_cast<unsigned>(num_seqs * HV), kSBlock, kStateSmem, st>>>(p, mk);
-  return cudaGetLastError() == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+  // a programmatic dependent of the prep kernel (when there is one): its CTAs start on
+  // the SMs the prep grid's tail leaves free
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(num_seqs * HV));
+  cfg.blockDim = dim3(kSBlock);
+  cfg.dynamicSmemBytes = kStateSmem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = total_tokens > 0 ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gdn_wy_state_kernel, p, mk) == cudaSuccess ? GDN_OK
+                                                                             : GDN_ERR_LAUNCH;
 }
 
 }  // extern "C"

@@ -10,7 +10,7 @@ larger than the 126 MB L2 is zeroed before every launch.
 
 from __future__ import annotations
 
-from typing import Callable, Dict, List, Optional
+from typing import Callable, Dict, List, Optional, Tuple
 
 import torch
 
@@ -48,11 +48,11 @@ def cupti_kernel_durations_us(fn: Callable[[], object], iters: int, device,
     return out
 
 
-def cupti_kernels_by_name(fn: Callable[[], object], iters: int, device,
-                          flush: Optional[Callable[[], object]] = None) -> Dict[str, List[float]]:
-    """Device durations (µs) of every kernel launched by ``iters`` calls of ``fn``,
-    grouped by kernel name; kernels that ``flush`` launches (it runs before every
-    call, inside the profiled region) are left out by name."""
+def _kernel_records(fn: Callable[[], object], iters: int, device,
+                    flush: Optional[Callable[[], object]] = None) -> List[Tuple[str, int, int]]:
+    """(name, start ns, end ns) of every kernel launched by ``iters`` calls of ``fn``,
+    in start order; kernels that ``flush`` launches (it runs before every call, inside
+    the profiled region) are left out by name."""
     from torch.profiler import ProfilerActivity, profile
 
     flush_names = set()
@@ -70,7 +70,7 @@ def cupti_kernels_by_name(fn: Callable[[], object], iters: int, device,
                 flush()
             fn()
         torch.cuda.synchronize(device)
-    out: Dict[str, List[float]] = {}
+    out = []
     for e in prof.profiler.kineto_results.events():
         if not str(e.device_type()).endswith("CUDA") or e.name() in flush_names:
             continue
@@ -78,5 +78,48 @@ def cupti_kernels_by_name(fn: Callable[[], object], iters: int, device,
             continue
         if "Memcpy" in e.name() or "Memset" in e.name():
             continue
-        out.setdefault(e.name(), []).append(e.duration_ns() / 1e3)
+        out.append((e.name(), e.start_ns(), e.start_ns() + e.duration_ns()))
+    out.sort(key=lambda r: r[1])
     return out
+
+
+def cupti_kernels_by_name(fn: Callable[[], object], iters: int, device,
+                          flush: Optional[Callable[[], object]] = None) -> Dict[str, List[float]]:
+    """Device durations (µs) of every kernel launched by ``iters`` calls of ``fn``,
+    grouped by kernel name; kernels that ``flush`` launches are left out by name."""
+    out: Dict[str, List[float]] = {}
+    for name, t0, t1 in _kernel_records(fn, iters, device, flush):
+        out.setdefault(name, []).append((t1 - t0) / 1e3)
+    return out
+
+
+def cupti_kernels_and_spans(fn: Callable[[], object], iters: int, device,
+                            flush: Optional[Callable[[], object]] = None,
+                            name_part: str = "gdn_"):
+    """``cupti_kernels_by_name``'s durations plus, for calls that launch several kernels
+    whose names contain ``name_part`` (each once per call), the span of each call from its
+    first kernel's start to its last kernel's end, in µs.  Summing the kernels' durations
+    would count twice the time in which a call's kernels overlap (a programmatic
+    dependent launched during its predecessor's tail); the span does not.  The spans are
+    None when the records do not split into whole calls."""
+    recs = _kernel_records(fn, iters, device, flush)
+    by_name: Dict[str, List[float]] = {}
+    for name, t0, t1 in recs:
+        by_name.setdefault(name, []).append((t1 - t0) / 1e3)
+    return by_name, call_spans_us(recs, name_part)
+
+
+def call_spans_us(recs: List[Tuple[str, int, int]], name_part: str = "gdn_"
+                  ) -> Optional[List[float]]:
+    """Per-call spans (µs) of (name, start ns, end ns) records in start order, for calls
+    that launch each kernel whose name contains ``name_part`` exactly once: consecutive
+    groups of as many records as there are such names, each group one call.  None when
+    the records do not split into whole calls (a dropped or extra record)."""
+    mine = [r for r in recs if name_part in r[0]]
+    k = len({r[0] for r in mine})
+    if k == 0 or len(mine) % k != 0:
+        return None
+    groups = [mine[i:i + k] for i in range(0, len(mine), k)]
+    if not all(len({r[0] for r in g}) == k for g in groups):
+        return None
+    return [(max(r[2] for r in g) - min(r[1] for r in g)) / 1e3 for g in groups]

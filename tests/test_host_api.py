@@ -87,6 +87,22 @@ def test_prefill_offsets_int32_pass_through_int64_clamped(monkeypatch):
     assert cu.dtype == torch.int32 and cu.tolist() == [0, 8, 8]
 
 
+def test_call_spans_from_overlapping_kernels():
+    """A call whose second kernel starts during its first one's tail is timed from the
+    first start to the last end (2 + 8 = 10 us summed, 9 us spanned); a dropped record
+    leaves no whole calls and gives None; other kernels (the L2 flush) are ignored."""
+    from gdn_b200.timing import call_spans_us
+
+    us = 1000
+    recs = [("gdn_a", 0, 2 * us), ("flush", 2 * us, 3 * us), ("gdn_b", 1 * us, 9 * us),
+            ("gdn_a", 20 * us, 22 * us), ("gdn_b", 21 * us, 25 * us)]
+    recs.sort(key=lambda r: r[1])
+    assert call_spans_us(recs) == [9.0, 5.0]
+    assert call_spans_us(recs[:-1]) is None
+    assert call_spans_us([("gdn_x", 0, 3 * us)]) == [3.0]
+    assert call_spans_us([("other", 0, 1)]) is None
+
+
 def test_scale_default():
     assert ops._resolve_scale(None, 128) == 1 / math.sqrt(128)
     assert ops._resolve_scale(0.0, 128) == 1 / math.sqrt(128)
